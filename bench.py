@@ -1,0 +1,494 @@
+"""Benchmark: mask-aware attention TFLOP/s on B200, 1..8 GPUs.
+
+Workload: non-softmax attention, B=32, H=32, S=8192,
+D=128, bf16, non-causal -- sigmoid(QK^T/sqrt(D) - log S) V and
+ReLU(QK^T/sqrt(D)) V / S. One step runs both operators over this rank's shard
+of the B*H = 1024 independent (batch, head) units; the units are split
+evenly across ranks (no collective on the data path), so total work is fixed
+as N grows ("strong" scaling).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+FLOPs are mask-aware: 4 * D * visible_pairs * units (masked pairs never
+count). Timing: W warm-up steps, then K steps between a barrier +
+synchronize on both sides, CUDA events on the launching stream, max over
+ranks. Inputs (6.4 GB per GPU at N=1) exceed the 126 MB L2, so no flush is
+needed between steps. Rank 0 prints one JSON line.
+
+``--impl reference`` times the reference's eager CPU implementation (the
+fp32 restatement in ``oracle/``, the reference's algorithm on the host cores,
+all threads) on a bounded sample of the same workload and prints the same
+JSON line with ``"impl": "reference"``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+B_TOTAL, H_TOTAL, S, D = 32, 32, 8192, 128
+SPEC_BF16_TFLOPS = 2250.0
+FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+METRIC = "mask-aware attention TFLOP/s (sigmoid + ReLU, config 5)"
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as fh:
+            d = json.load(fh)
+        return {k: float(d[k]) for k in FALLBACK if k in d}, "measured"
+    return dict(FALLBACK), "fallback"
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def shard(units: int, ws: int, rank: int):
+    """Contiguous, even split of ``units`` (batch*head pairs) over ``ws`` ranks."""
+    lo = units * rank // ws
+    hi = units * (rank + 1) // ws
+    return lo, hi
+
+
+def variants():
+    import chia_proj_b200 as cp
+    return [
+        ("sigmoid_attn", lambda q, k, v: cp.sigmoid_attn(q, k, v, causal=False, bias=-math.log(S)),
+         dict(causal=False, bias=-math.log(S))),
+        ("relu_attn", lambda q, k, v: cp.relu_attn(q, k, v, causal=False, out_scale=1.0 / S),
+         dict(causal=False, out_scale=1.0 / S)),
+    ]
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML during a region."""
+
+    REASONS = {
+        "gpu_idle": 0x1, "applications_clocks_setting": 0x2, "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8, "sync_boost": 0x10, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+        "display_clock_setting": 0x100,
+    }
+
+    def __init__(self, index: int, period_s: float = 0.1):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # pragma: no cover - NVML absent
+            self._nv = None
+        self.period = period_s
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for name, bit in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t is not None:
+            self._t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"]}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons - {"gpu_idle"}), "samples": len(self.samples)}
+
+
+# --------------------------------------------------------------- GPU arm
+def make_inputs(n_units: int, device, seed: int):
+    """Seeded N(0,1) bf16 inputs for this rank's units, generated on device."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    shp = (1, n_units, S, D)
+    return [torch.randn(shp, generator=g, device=device, dtype=torch.float32).to(torch.bfloat16)
+            for _ in range(3)]
+
+
+def traffic_from_profile(kernel: str):
+    """DRAM bytes per launch from the committed ncu summary, if present."""
+    p = os.path.join(ROOT, "profiles", f"{kernel}_config5.txt")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch_full:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def cpu_oracle_sample(target_s: float, max_units: int):
+    """Time the oracle (reference algorithm, fp32, host cores) on a sample of units."""
+    import oracle
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(1234)
+    vs = variants()
+    flops_unit = 2 * 4 * D * S * S  # both operators, full mask
+    # one unit first, to size the sample
+    q, k, v = (torch.randn(1, 1, S, D, generator=g).to(torch.bfloat16) for _ in range(3))
+    t0 = time.perf_counter()
+    for name, _, kw in vs:
+        oracle.run_op(name, q, k, v, **kw)
+    one = time.perf_counter() - t0
+    n = max(1, min(max_units, int(target_s / max(one, 1e-3))))
+    q, k, v = (torch.randn(1, n, S, D, generator=g).to(torch.bfloat16) for _ in range(3))
+    t0 = time.perf_counter()
+    outs = {name: oracle.run_op(name, q, k, v, **kw) for name, _, kw in vs}
+    dt = time.perf_counter() - t0
+    return {"value": flops_unit * n / dt / 1e12, "unit": "TFLOP/s",
+            "cores": torch.get_num_threads(), "sample_units": n, "seconds": dt,
+            "sample": f"{n} of {B_TOTAL * H_TOTAL} (batch, head) units of config 5, both operators, "
+                      f"fp32 eager restatement on the host CPU"}, (q, k, v, outs)
+
+
+def headline_suite(device):
+    """All ten operators at the north-star shape B4 H16 S4096 D128 (+ configs 2, 3)."""
+    import chia_proj_b200 as cp
+    g = torch.Generator(device=device).manual_seed(7)
+    out = {}
+
+    def bench_one(fn, q, k, v, mask, B, H, Sx, Dx, elem, iters=10):
+        for _ in range(3):
+            fn(q, k, v)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        for _ in range(iters):
+            fn(q, k, v)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        fl = cp.mask_aware_flops(mask, B, H, Sx, Dx)
+        by = 4 * B * H * Sx * Dx * elem
+        return {"us": round(ms * 1e3, 1), "tflops": round(fl / ms / 1e9, 1),
+                "pct_spec_peak": round(100 * fl / ms / 1e9 / SPEC_BF16_TFLOPS, 1),
+                "hbm_gbs": round(by / ms / 1e6, 1)}
+
+    B, H, Sx, Dx = 4, 16, 4096, 128
+    q, k, v = (torch.randn(B, H, Sx, Dx, generator=g, device=device).to(torch.bfloat16)
+               for _ in range(3))
+    gh = torch.Generator().manual_seed(0)
+    tau = 0.5 + 1.5 * torch.rand(H, generator=gh)
+    suite = {
+        "softcap_gemma2": (lambda q, k, v: cp.softcap_gemma2(q, k, v, cap=50.0), cp.CAUSAL,
+                           "cap 50, causal"),
+        "bias_sliding_window": (cp.bias_sliding_window, cp.op_config("bias_sliding_window"),
+                                "window 256"),
+        "bias_local": (cp.bias_local, cp.op_config("bias_local"), "|i-j|<256"),
+        "bias_alibi": (lambda q, k, v: cp.bias_alibi(q, k, v, slopes=cp.alibi_slopes_geometric(H)),
+                       cp.CAUSAL, "slopes 2^(-8(h+1)/H), causal"),
+        "bias_block_diagonal": (lambda q, k, v: cp.bias_block_diagonal(q, k, v, block=256),
+                                cp.op_config("bias_block_diagonal", block=256), "block 256, causal"),
+        "bias_dilated": (cp.bias_dilated, cp.op_config("bias_dilated"), "dilation 4, causal"),
+        "bias_prefix_lm": (lambda q, k, v: cp.bias_prefix_lm(q, k, v, prefix=1024),
+                           cp.op_config("bias_prefix_lm", prefix=1024), "prefix 1024"),
+        "temp_perhead": (lambda q, k, v: cp.temp_perhead(q, k, v, temps=1.0 / tau), cp.CAUSAL,
+                         "1/tau_h, tau ~ U[0.5,2], causal"),
+        "sigmoid_attn": (lambda q, k, v: cp.sigmoid_attn(q, k, v, causal=False,
+                                                         bias=-math.log(Sx)), cp.FULL,
+                         "bias -log S, non-causal"),
+        "relu_attn": (lambda q, k, v: cp.relu_attn(q, k, v, causal=False, out_scale=1.0 / Sx),
+                      cp.FULL, "1/S, non-causal"),
+    }
+    shape = {"B": B, "H": H, "S": Sx, "D": Dx, "dtype": "bf16"}
+    out["headline"] = {"shape": shape, "variants": {
+        name: {**bench_one(fn, q, k, v, m, B, H, Sx, Dx, 2), "params": desc}
+        for name, (fn, m, desc) in suite.items()}}
+    del q, k, v
+    # config 2: window 256, D=64
+    B2, H2, S2, D2 = 4, 16, 2048, 64
+    q, k, v = (torch.randn(B2, H2, S2, D2, generator=g, device=device).to(torch.bfloat16)
+               for _ in range(3))
+    out["config2"] = {"shape": {"B": B2, "H": H2, "S": S2, "D": D2, "dtype": "bf16"},
+                      "bias_sliding_window": bench_one(cp.bias_sliding_window, q, k, v,
+                                                       cp.op_config("bias_sliding_window"),
+                                                       B2, H2, S2, D2, 2)}
+    del q, k, v
+    # config 3: fp16 ALiBi / temperature, B8 H32 S4096 D128
+    B3, H3 = 8, 32
+    q, k, v = (torch.randn(B3, H3, 4096, 128, generator=g, device=device).to(torch.float16)
+               for _ in range(3))
+    tau3 = 0.5 + 1.5 * torch.rand(H3, generator=gh)
+    out["config3"] = {"shape": {"B": B3, "H": H3, "S": 4096, "D": 128, "dtype": "fp16"},
+                      "bias_alibi": bench_one(
+                          lambda q, k, v: cp.bias_alibi(q, k, v,
+                                                        slopes=cp.alibi_slopes_geometric(H3)),
+                          q, k, v, cp.CAUSAL, B3, H3, 4096, 128, 2, iters=5),
+                      "temp_perhead": bench_one(
+                          lambda q, k, v: cp.temp_perhead(q, k, v, temps=1.0 / tau3),
+                          q, k, v, cp.CAUSAL, B3, H3, 4096, 128, 2, iters=5)}
+    del q, k, v
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_ours(a):
+    import torch.distributed as dist
+
+    import chia_proj_b200 as cp
+
+    ws, rank, local = dist_env()
+    assert ws == a.gpus, f"--gpus {a.gpus} but WORLD_SIZE {ws}"
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=device)
+    units = a.units
+    lo, hi = shard(units, ws, rank)
+    n = hi - lo
+    q, k, v = make_inputs(n, device, seed=1000 + rank)
+    outs = {}
+    vs = variants()
+    fl_unit = 4 * D * cp.visible_pairs(cp.FULL, S)
+    flops_step_rank = fl_unit * n * len(vs)
+    flops_step_total = fl_unit * units * len(vs)
+    stream = torch.cuda.current_stream(device)
+
+    def step(events=None):
+        for vi, (name, fn, _) in enumerate(vs):
+            if events is not None:
+                events[vi][0].record(stream)
+            outs[name] = fn(q, k, v)
+            if events is not None:
+                events[vi][1].record(stream)
+
+    def barrier():
+        if ws > 1:
+            dist.barrier()
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    cp.check_device_status(local)
+
+    ev = [[[torch.cuda.Event(True), torch.cuda.Event(True)] for _ in vs] for _ in range(a.steps)]
+    e_start, e_end = torch.cuda.Event(True), torch.cuda.Event(True)
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        e_start.record(stream)
+        for s in range(a.steps):
+            step(ev[s])
+        e_end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ms = e_start.elapsed_time(e_end)
+    per_kernel_ms = {name: statistics.mean(ev[s][vi][0].elapsed_time(ev[s][vi][1])
+                                           for s in range(a.steps))
+                     for vi, (name, _, _) in enumerate(vs)}
+    cp.check_device_status(local)
+
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    if ws > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = flops_step_total * a.steps / (ms_max * 1e-3) / 1e12
+
+    # ---- verification: one unit per rank against an fp32 torch reference,
+    # errors gathered to rank 0 after timing (the only collective)
+    with torch.no_grad():
+        errs = []
+        for name, _, kw in vs:
+            qf, kf, vf = (x[0, 0].float() for x in (q, k, v))
+            s_ = (qf @ kf.t()) / math.sqrt(D)
+            p_ = torch.sigmoid(s_ + kw["bias"]) if name == "sigmoid_attn" else \
+                torch.relu(s_) * kw["out_scale"]
+            ref = p_ @ vf
+            errs.append((outs[name][0, 0].float() - ref).abs().max().item())
+            del s_, p_, ref
+    e = torch.tensor(errs, dtype=torch.float64, device=device)
+    if ws > 1:
+        gathered = [torch.zeros_like(e) for _ in range(ws)]
+        dist.all_gather(gathered, e)
+        e = torch.stack(gathered).max(0).values
+    verify = {name: float(e[i]) for i, (name, _, _) in enumerate(vs)}
+
+    # ---- end to end through the public API, host buffers, every step
+    e2e = None
+    if not a.no_e2e:
+        hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+        host_out = {name: torch.empty(q.shape, dtype=q.dtype).pin_memory() for name, _, _ in vs}
+        del q, k, v
+        outs.clear()
+        torch.cuda.empty_cache()
+        e2e_steps = max(1, min(a.steps, 3))
+
+        def e2e_step():
+            dq, dk, dv = (x.to(device, non_blocking=True) for x in (hq, hk, hv))
+            for name, fn, _ in vs:
+                host_out[name].copy_(fn(dq, dk, dv), non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        t2 = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
+        if ws > 1:
+            dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t2.item())
+        bi = 3 * hq.numel() * hq.element_size()
+        bo = len(vs) * hq.numel() * hq.element_size()
+        e2e = {"value": round(flops_step_total * e2e_steps / (e2e_ms * 1e-3) / 1e12, 2),
+               "unit": "TFLOP/s", "h2d_bytes_per_step": bi, "d2h_bytes_per_step": bo,
+               "steps": e2e_steps, "path": "chia_proj_b200.sigmoid_attn / relu_attn with pinned "
+                                           "host inputs copied in and outputs copied out"}
+
+    result = None
+    if rank == 0:
+        pk, src = peaks()
+        dom = max(per_kernel_ms, key=per_kernel_ms.get)
+        achieved = fl_unit * n / (per_kernel_ms[dom] * 1e-3) / 1e12
+        peak = pk.get("bf16_tflops_sustained", FALLBACK["bf16_tflops_sustained"])
+        traffic = traffic_from_profile(dom)
+        result = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": ws,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_max / a.steps, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic: seeded N(0,1) q, k, v (no dataset in the reference)",
+            "config": {"workload": "config 5: sigmoid(s - log S) and ReLU(s)/S attention, "
+                                   "non-causal", "B": B_TOTAL, "H": H_TOTAL, "S": S, "D": D,
+                       "units_total": units,
+                       "units_per_gpu": n, "parallelism": f"bxh-shard{ws}",
+                       "l2": "inputs 6.4 GB/N per GPU > 126 MB L2, no flush needed"},
+            "variants": {name: {"ms_per_launch": round(per_kernel_ms[name], 3),
+                                "tflops_per_gpu": round(fl_unit * n / per_kernel_ms[name] / 1e9, 1),
+                                "pct_spec_bf16_peak": round(100 * fl_unit * n / per_kernel_ms[name]
+                                                            / 1e9 / SPEC_BF16_TFLOPS, 1),
+                                "verify_max_abs": verify[name]}
+                         for name, _, _ in vs},
+            "roofline": {"bound": "tensor", "kernel": dom, "achieved": round(achieved, 1),
+                         "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                         "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a "
+                                        f"seconds-long region)",
+                         "frac_of_spec_2250": round(achieved / SPEC_BF16_TFLOPS, 4),
+                         "traffic": traffic},
+            "clocks": clk.summary(),
+            "gpu_launches": len(vs) * a.steps,
+            "e2e": e2e,
+        }
+    if ws > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        if ws == 1 and not a.no_cpu_baseline:
+            cpu, _ = cpu_oracle_sample(target_s=a.cpu_seconds, max_units=16)
+            result["cpu_baseline"] = {**cpu, "kind": "port"}
+        if ws == 1 and not a.no_suite:
+            result["suite"] = headline_suite(device)
+        print(json.dumps(result), flush=True)
+
+
+# ------------------------------------------------------------ reference arm
+def run_reference(a):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    import oracle
+    torch.set_num_threads(os.cpu_count() or 1)
+    vs = variants()
+    g = torch.Generator().manual_seed(99)
+    q, k, v = (torch.randn(1, 1, S, D, generator=g).to(torch.bfloat16) for _ in range(3))
+    fl_unit = 2 * 4 * D * S * S
+
+    def one_step(n):
+        t0 = time.perf_counter()
+        for i in range(n):
+            for name, _, kw in vs:
+                oracle.run_op(name, q, k, v, **kw)
+        return time.perf_counter() - t0
+
+    t1 = one_step(1)
+    n = max(1, min(16, int(a.ref_step_seconds / max(t1, 1e-3))))
+    for _ in range(max(0, a.warmup - 1)):
+        one_step(n)
+    times = [one_step(n) for _ in range(a.steps)]
+    dt = sum(times) / len(times)
+    value = fl_unit * n / dt / 1e12
+    sample = (f"{n} (batch, head) unit(s) of config 5 per step (both operators, S=8192, D=128), "
+              f"fp32 eager restatement of the reference on the host CPU")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s",
+        "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(dt * 1e3, 1),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded N(0,1)",
+        "config": {"workload": "config 5: sigmoid(s - log S) and ReLU(s)/S attention, non-causal",
+                   "B": B_TOTAL, "H": H_TOTAL, "S": S, "D": D},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s",
+                         "cores": torch.get_num_threads(), "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-suite", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--ref-step-seconds", type=float, default=3.0)
+    ap.add_argument("--units", type=int, default=B_TOTAL * H_TOTAL,
+                    help="(batch, head) units in the job; smaller values are for ncu captures")
+    a = ap.parse_args(argv)
+    if a.warmup < 3 and a.impl == "ours":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

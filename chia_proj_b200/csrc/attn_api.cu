@@ -1,0 +1,300 @@
+// attn_api.cu -- extern "C" entry points of libchia_attn.so (include/chia_attn.h).
+//
+// Host responsibilities: validate arguments (errors are returned before any
+// launch), turn the mask fields into MaskGeom, pick the kernel
+// instantiation (head_dim x dtype x kind), encode the three TMA tensor maps
+// and launch on the caller's stream. No allocation, no synchronisation.
+//
+// Dilated masks take a residue-class fast path when it is exact: with
+// dilation d, query i only sees keys j == i (mod d), so the problem splits
+// into d independent problems over rows r, r+d, r+2d, ... . Each becomes a
+// "virtual head" whose rows are read by TMA with a row stride of d rows, and
+// whose mask is the same band divided by d. None of its tiles is then 3/4
+// masked, unlike the plain causal path with an element-wise (i-j)%d test.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/chia_attn.h"
+#include "fmha_sm100.cuh"
+
+namespace {
+
+using chia::MaskGeom;
+
+constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;  // 2 s per barrier wait
+
+struct Derived {
+  MaskGeom geom;  // in virtual index space
+  int vdil;       // 1, or d for the dilated fast path
+};
+
+int derive(const chia_attn_params_t *p, Derived &out) {
+  if (p->win_left < -1 || p->win_right < -1 || p->block < 0 || p->prefix < 0 ||
+      p->dilation < 1)
+    return CHIA_ERR_INVALID_ARGUMENT;
+  MaskGeom g{};
+  g.sq = p->seqlen_q;
+  g.skv = p->seqlen_kv;
+  g.left = p->win_left;
+  g.right = p->win_right;
+  g.block = p->block;
+  g.prefix = p->prefix < p->seqlen_kv ? p->prefix : p->seqlen_kv;
+  g.dil = p->dilation;
+  out.vdil = 1;
+  const int64_t d = p->dilation;
+  if (d > 1 && g.block == 0 && g.prefix == 0 && g.sq % d == 0 && g.skv % d == 0) {
+    // i = i' d + r, j = j' d + r  =>  i - j = (i' - j') d
+    g.sq /= d;
+    g.skv /= d;
+    if (g.left >= 0) g.left /= d;
+    if (g.right >= 0) g.right /= d;
+    g.dil = 1;
+    out.vdil = static_cast<int>(d);
+  }
+  out.geom = g;
+  return CHIA_OK;
+}
+
+// Host-side mask geometry in REAL index space (for counting and planning).
+MaskGeom real_geom(const chia_attn_params_t *p) {
+  MaskGeom g{};
+  g.sq = p->seqlen_q;
+  g.skv = p->seqlen_kv;
+  g.left = p->win_left;
+  g.right = p->win_right;
+  g.block = p->block;
+  g.prefix = p->prefix < p->seqlen_kv ? p->prefix : p->seqlen_kv;
+  g.dil = p->dilation;
+  return g;
+}
+
+bool aligned16(const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+int validate(const chia_attn_params_t *p) {
+  if (p == nullptr) return CHIA_ERR_INVALID_ARGUMENT;
+  if (p->abi_version != CHIA_ATTN_ABI_VERSION) return CHIA_ERR_INVALID_ARGUMENT;
+  if (p->dtype != CHIA_DTYPE_BF16 && p->dtype != CHIA_DTYPE_F16) return CHIA_ERR_UNSUPPORTED;
+  if (p->head_dim != 64 && p->head_dim != 128) return CHIA_ERR_UNSUPPORTED;
+  if (p->norm < CHIA_NORM_SOFTMAX || p->norm > CHIA_NORM_RELU) return CHIA_ERR_INVALID_ARGUMENT;
+  if (p->mod < CHIA_MOD_NONE || p->mod > CHIA_MOD_TEMP) return CHIA_ERR_INVALID_ARGUMENT;
+  if (p->norm != CHIA_NORM_SOFTMAX && p->mod != CHIA_MOD_NONE) return CHIA_ERR_UNSUPPORTED;
+  if (p->batch < 1 || p->heads < 1 || p->seqlen_q < 1 || p->seqlen_kv < 1)
+    return CHIA_ERR_INVALID_ARGUMENT;
+  if (p->seqlen_q > (int64_t(1) << 30) || p->seqlen_kv > (int64_t(1) << 30) ||
+      p->heads > (int64_t(1) << 24) || p->batch > (int64_t(1) << 24))
+    return CHIA_ERR_UNSUPPORTED;
+  if (!p->q || !p->k || !p->v || !p->o) return CHIA_ERR_INVALID_ARGUMENT;
+  if ((p->mod == CHIA_MOD_ALIBI || p->mod == CHIA_MOD_TEMP) && p->head_param == nullptr)
+    return CHIA_ERR_INVALID_ARGUMENT;
+  if (p->mod == CHIA_MOD_SOFTCAP && !(p->softcap > 0.f)) return CHIA_ERR_INVALID_ARGUMENT;
+  if (!std::isfinite(p->scale) || !std::isfinite(p->sig_bias) || !std::isfinite(p->out_scale))
+    return CHIA_ERR_INVALID_ARGUMENT;
+  if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->o))
+    return CHIA_ERR_MISALIGNED;
+  const int64_t *strides[4] = {p->q_stride, p->k_stride, p->v_stride, p->o_stride};
+  for (auto *s : strides)
+    for (int d = 0; d < 3; ++d) {
+      if (s[d] < 0) return CHIA_ERR_INVALID_ARGUMENT;
+      if (s[d] % 8 != 0) return CHIA_ERR_MISALIGNED;  // 16-byte TMA stride rule
+    }
+  Derived dv;
+  return derive(p, dv);
+}
+
+// ----------------------------------------------------------------- TMA maps
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// 5-D view (D, S', vdil, H, B) of a [B, H, S, D] tensor; box (64, 128, 1, 1, 1),
+// 128-byte swizzle, zero fill out of bounds.
+bool encode_map(CUtensorMap *map, const void *base, int dtype, int64_t D, int64_t s_virtual,
+                int vdil, int64_t H, int64_t B, const int64_t *stride_el) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[5] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(s_virtual),
+                              static_cast<cuuint64_t>(vdil), static_cast<cuuint64_t>(H),
+                              static_cast<cuuint64_t>(B)};
+  const cuuint64_t strides[4] = {static_cast<cuuint64_t>(stride_el[2] * vdil * 2),
+                                 static_cast<cuuint64_t>(stride_el[2] * 2),
+                                 static_cast<cuuint64_t>(stride_el[1] * 2),
+                                 static_cast<cuuint64_t>(stride_el[0] * 2)};
+  const cuuint32_t box[5] = {64, 128, 1, 1, 1};
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  const CUtensorMapDataType dt =
+      dtype == CHIA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  // strides of size-1 dims must still be valid multiples of 16; a zero stride
+  // (broadcast) is replaced by the next one, which it never affects.
+  cuuint64_t st[4];
+  for (int d = 0; d < 4; ++d) st[d] = strides[d] ? strides[d] : 16;
+  const CUresult r = fn(map, dt, 5, const_cast<void *>(base), dims, st, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// ----------------------------------------------------------------- dispatch
+template <int D, bool BF16, int KIND>
+int launch_one(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
+               const chia::KernelArgs &a, int64_t nblocks, cudaStream_t stream) {
+  using Cfg = chia::FmhaConfig<D>;
+  auto kern = chia::fmha_fwd_kernel<D, BF16, KIND>;
+  static std::atomic<uint32_t> configured{0};  // bit per device ordinal (< 32)
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHIA_ERR_NO_DEVICE;
+  const uint32_t bit = 1u << (dev & 31);
+  if (!(configured.load(std::memory_order_acquire) & bit)) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_ALLOC) !=
+        cudaSuccess)
+      return CHIA_ERR_LAUNCH;
+    // setmaxnreg.inc can only hand out registers the launch allocated: refuse
+    // to run a build whose register count cannot cover the warpgroup split.
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, kern) != cudaSuccess) return CHIA_ERR_LAUNCH;
+    if (fa.numRegs * Cfg::THREADS < 2 * 128 * Cfg::REG_SOFTMAX + 128 * Cfg::REG_OTHER)
+      return CHIA_ERR_UNSUPPORTED;
+    configured.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  kern<<<static_cast<unsigned>(nblocks), Cfg::THREADS, Cfg::SMEM_ALLOC, stream>>>(mq, mk, mv, a);
+  return cudaGetLastError() == cudaSuccess ? CHIA_OK : CHIA_ERR_LAUNCH;
+}
+
+template <int D, bool BF16>
+int launch_kind(int kind, const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
+                const chia::KernelArgs &a, int64_t nblocks, cudaStream_t s) {
+  switch (kind) {
+    case chia::KIND_SOFTMAX: return launch_one<D, BF16, chia::KIND_SOFTMAX>(mq, mk, mv, a, nblocks, s);
+    case chia::KIND_SOFTCAP: return launch_one<D, BF16, chia::KIND_SOFTCAP>(mq, mk, mv, a, nblocks, s);
+    case chia::KIND_ALIBI: return launch_one<D, BF16, chia::KIND_ALIBI>(mq, mk, mv, a, nblocks, s);
+    case chia::KIND_SIGMOID: return launch_one<D, BF16, chia::KIND_SIGMOID>(mq, mk, mv, a, nblocks, s);
+    case chia::KIND_RELU: return launch_one<D, BF16, chia::KIND_RELU>(mq, mk, mv, a, nblocks, s);
+  }
+  return CHIA_ERR_INVALID_ARGUMENT;
+}
+
+int kind_of(const chia_attn_params_t *p) {
+  if (p->norm == CHIA_NORM_SIGMOID) return chia::KIND_SIGMOID;
+  if (p->norm == CHIA_NORM_RELU) return chia::KIND_RELU;
+  switch (p->mod) {
+    case CHIA_MOD_SOFTCAP: return chia::KIND_SOFTCAP;
+    case CHIA_MOD_ALIBI: return chia::KIND_ALIBI;
+    default: return chia::KIND_SOFTMAX;  // NONE and TEMP (TEMP folds into the scale)
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int chia_attn_abi_version(void) { return CHIA_ATTN_ABI_VERSION; }
+
+const char *chia_attn_status_string(int status) {
+  switch (status) {
+    case CHIA_OK: return "ok";
+    case CHIA_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case CHIA_ERR_UNSUPPORTED: return "unsupported configuration";
+    case CHIA_ERR_MISALIGNED: return "pointer or stride not 16-byte aligned";
+    case CHIA_ERR_LAUNCH: return "kernel launch or tensor-map encoding failed";
+    case CHIA_ERR_DEVICE_TIMEOUT: return "bounded device wait expired";
+    case CHIA_ERR_NO_DEVICE: return "no usable sm_100 device";
+  }
+  return "unknown status";
+}
+
+int64_t chia_attn_visible_pairs(const chia_attn_params_t *p) {
+  if (p == nullptr || p->seqlen_q < 0 || p->seqlen_kv < 0 || p->win_left < -1 ||
+      p->win_right < -1 || p->block < 0 || p->prefix < 0 || p->dilation < 1)
+    return -1;
+  return chia::visible_pairs(real_geom(p));
+}
+
+int chia_attn_tile_plan(const chia_attn_params_t *p, int64_t row0, int32_t tile_m,
+                        int32_t tile_n, int64_t *tile_lo, int64_t *tile_hi,
+                        uint64_t *full_mask) {
+  if (p == nullptr || tile_m < 1 || tile_n < 1 || !tile_lo || !tile_hi || !full_mask || row0 < 0)
+    return CHIA_ERR_INVALID_ARGUMENT;
+  if (p->seqlen_q < 1 || p->seqlen_kv < 1 || p->win_left < -1 || p->win_right < -1 ||
+      p->block < 0 || p->prefix < 0 || p->dilation < 1)
+    return CHIA_ERR_INVALID_ARGUMENT;
+  const MaskGeom g = real_geom(p);
+  int64_t lo, hi;
+  chia::tile_range(g, row0, row0 + tile_m - 1, tile_n, lo, hi);
+  uint64_t m = 0;
+  for (int64_t t = lo; t < hi && t - lo < 64; ++t)
+    if (chia::tile_full(g, row0, row0 + tile_m - 1, tile_n, t)) m |= 1ull << (t - lo);
+  *tile_lo = lo;
+  *tile_hi = hi;
+  *full_mask = m;
+  return CHIA_OK;
+}
+
+int chia_attn_fwd(const chia_attn_params_t *p, void *stream) {
+  const int v = validate(p);
+  if (v != CHIA_OK) return v;
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHIA_ERR_NO_DEVICE;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      major != 10)
+    return CHIA_ERR_NO_DEVICE;
+
+  Derived dv;
+  derive(p, dv);
+  const MaskGeom &g = dv.geom;
+  const int D = p->head_dim;
+  CUtensorMap mq, mk, mv;
+  if (!encode_map(&mq, p->q, p->dtype, D, g.sq, dv.vdil, p->heads, p->batch, p->q_stride) ||
+      !encode_map(&mk, p->k, p->dtype, D, g.skv, dv.vdil, p->heads, p->batch, p->k_stride) ||
+      !encode_map(&mv, p->v, p->dtype, D, g.skv, dv.vdil, p->heads, p->batch, p->v_stride))
+    return CHIA_ERR_LAUNCH;
+
+  chia::KernelArgs a{};
+  a.mask = g;
+  a.heads = static_cast<int32_t>(p->heads);
+  a.vdil = dv.vdil;
+  const int64_t rows_per_cta = 2 * 128;
+  const int64_t nqb = (g.sq + rows_per_cta - 1) / rows_per_cta;
+  const int64_t nvh = p->batch * p->heads * dv.vdil;
+  const int64_t nblocks = nqb * nvh;
+  if (nblocks > 0x7fffffffLL || nqb > 0x7fffffffLL) return CHIA_ERR_UNSUPPORTED;
+  a.n_qblocks = static_cast<int32_t>(nqb);
+  a.n_vheads = static_cast<int32_t>(nvh);
+  a.score_scale = p->scale;
+  a.softcap = p->softcap;
+  a.sig_bias = p->sig_bias;
+  a.out_scale = p->out_scale;
+  a.head_param = (p->mod == CHIA_MOD_ALIBI || p->mod == CHIA_MOD_TEMP) ? p->head_param : nullptr;
+  a.o = p->o;
+  a.o_sb = p->o_stride[0];
+  a.o_sh = p->o_stride[1];
+  a.o_ss = p->o_stride[2];
+  a.status = p->status;
+  a.timeout_ns = kDefaultTimeoutNs;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int kind = kind_of(p);
+  const bool bf16 = p->dtype == CHIA_DTYPE_BF16;
+  if (D == 128)
+    return bf16 ? launch_kind<128, true>(kind, mq, mk, mv, a, nblocks, s)
+                : launch_kind<128, false>(kind, mq, mk, mv, a, nblocks, s);
+  return bf16 ? launch_kind<64, true>(kind, mq, mk, mv, a, nblocks, s)
+              : launch_kind<64, false>(kind, mq, mk, mv, a, nblocks, s);
+}
+
+}  // extern "C"

@@ -1,0 +1,362 @@
+"""The ten attention operators, with the reference's eager call signatures.
+
+Each function takes ``q, k, v`` of shape ``[B, H, S, D]`` on a B200 and
+returns ``out`` of the same shape and dtype, exactly like the reference's
+eager closures in ``build_refs()`` (JoshiP-commits/CHIA_proj
+``extra_bench.py:32-62``; corrected sigmoid ``sigmoid_fix.py:34-40``) and its
+plugin entry point ``launch_kernel(q, k, v)`` (``extra_bench.py:24-27``).
+Keyword arguments default to the reference's hardcoded values; the benchmark
+configurations change them (softcap 50 non-causal, geometric ALiBi slopes,
+block 256, prefix 1024, sigmoid bias -log S, ReLU scale 1/S, ...).
+
+All computation happens in ``libchia_attn.so`` (one sm_100a kernel launch per
+call, on the current CUDA stream). There is no CPU or PyTorch fallback: CPU
+tensors raise, a missing library raises.
+
+Numerics: q.k and P.V run on the tensor cores with fp32 accumulation; the
+score modification, mask and normaliser run in fp32; P is rounded to the
+input dtype before P.V, as the reference's ``p.to(DT) @ v`` does
+(``extra_bench.py:45``). fp32 inputs are accepted for signature
+compatibility and computed in bf16 (the tensor-core input type), output
+returned in fp32.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+from typing import Dict, Optional, Sequence, Union
+
+import torch
+
+from . import _native as N
+
+__all__ = [
+    "Mask", "CAUSAL", "FULL", "attention", "OPS", "op_config", "visible_pairs",
+    "softcap_gemma2", "bias_sliding_window", "bias_local", "bias_alibi",
+    "bias_block_diagonal", "bias_dilated", "bias_prefix_lm", "temp_perhead",
+    "sigmoid_attn", "relu_attn", "alibi_slopes_geometric", "reference_alibi_slopes",
+    "reference_temps", "check_device_status",
+]
+
+
+@dataclass(frozen=True)
+class Mask:
+    """Visibility of key j for query i (``include/chia_attn.h``).
+
+    ``vis = j < prefix or (i-j <= left [left>=0] and j-i <= right [right>=0]
+    and same block [block>0] and (i-j) % dilation == 0)``.
+    """
+
+    left: int = -1
+    right: int = 0
+    block: int = 0
+    prefix: int = 0
+    dilation: int = 1
+
+    def validate(self) -> "Mask":
+        if self.left < -1 or self.right < -1 or self.block < 0 or self.prefix < 0 \
+                or self.dilation < 1:
+            raise ValueError(f"invalid mask {self}")
+        return self
+
+
+CAUSAL = Mask(left=-1, right=0)
+FULL = Mask(left=-1, right=-1)
+
+_NORMS = {"softmax": N.NORM_SOFTMAX, "sigmoid": N.NORM_SIGMOID, "relu": N.NORM_RELU}
+_MODS = {"none": N.MOD_NONE, "softcap": N.MOD_SOFTCAP, "alibi": N.MOD_ALIBI,
+         "temp": N.MOD_TEMP}
+
+_status_words: Dict[int, torch.Tensor] = {}
+_param_cache: Dict[tuple, torch.Tensor] = {}
+
+
+def _status_word(device: torch.device) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _status_words.get(idx)
+    if t is None:
+        t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status_words[idx] = t
+    return t
+
+
+def check_device_status(device: Optional[Union[int, torch.device]] = None) -> None:
+    """Synchronise ``device`` and raise if any kernel there reported an error.
+
+    Kernels OR error codes (a bounded wait that expired) into a per-device
+    status word instead of trapping; this reads and clears it.
+    """
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       (device if isinstance(device, int) else device.index))
+    w = _status_word(dev)
+    code = int(w.item())
+    if code:
+        w.zero_()
+        raise N.ChiaError(code, "reported by a kernel on " + str(dev))
+
+
+def _param_tensor(values, H: int, device: torch.device) -> torch.Tensor:
+    if isinstance(values, torch.Tensor):
+        t = values.detach().to(device=device, dtype=torch.float32).contiguous()
+    else:
+        t = torch.tensor(list(values), dtype=torch.float32, device=device)
+    if t.numel() != H:
+        raise ValueError(f"per-head parameter must have {H} entries, got {t.numel()}")
+    return t
+
+
+def reference_alibi_slopes(H: int) -> torch.Tensor:
+    """ALiBi slopes of the reference, ``h+1`` (``extra_bench.py:36``)."""
+    return torch.arange(1, H + 1, dtype=torch.float32)
+
+
+def alibi_slopes_geometric(H: int) -> torch.Tensor:
+    """Geometric ALiBi slopes ``2^(-8(h+1)/H)`` (the benchmark configuration)."""
+    return torch.pow(2.0, -8.0 * (torch.arange(H, dtype=torch.float32) + 1) / H)
+
+
+def reference_temps(H: int) -> torch.Tensor:
+    """Per-head multipliers of the reference, ``0.5+h/H`` (``extra_bench.py:35``)."""
+    return 0.5 + torch.arange(H, dtype=torch.float32) / H
+
+
+def _cached_default(kind: str, H: int, device: torch.device) -> torch.Tensor:
+    key = (kind, H, str(device))
+    t = _param_cache.get(key)
+    if t is None:
+        src = reference_alibi_slopes(H) if kind == "alibi" else reference_temps(H)
+        t = src.to(device)
+        _param_cache[key] = t
+    return t
+
+
+def _prep(x: torch.Tensor) -> torch.Tensor:
+    """Make a tensor TMA-compatible: unit last stride, 16-byte aligned rows."""
+    if x.stride(-1) != 1 or any(s % 8 for s in x.stride()[:-1]) or x.data_ptr() % 16:
+        x = x.contiguous()
+    return x
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
+              norm: str = "softmax", mod: str = "none", mask: Mask = CAUSAL,
+              scale: Optional[float] = None, softcap: float = 30.0,
+              head_param: Optional[Union[torch.Tensor, Sequence[float]]] = None,
+              sig_bias: float = 0.0, out_scale: float = 1.0,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Generic forward attention: ``norm(mask(mod(q.k * scale))) @ v``.
+
+    ``q, k, v``: CUDA tensors ``[B, H, S, D]`` (bf16 / fp16; fp32 computed as
+    bf16), ``D`` in {64, 128}. ``head_param``: ALiBi slopes (``mod="alibi"``)
+    or logit multipliers (``mod="temp"``), one per head.
+    """
+    if norm not in _NORMS or mod not in _MODS:
+        raise ValueError(f"unknown norm/mod {norm!r}/{mod!r}")
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if not isinstance(t, torch.Tensor) or t.dim() != 4:
+            raise ValueError(f"{name} must be a [B, H, S, D] tensor")
+        if t.device.type != "cuda":
+            raise RuntimeError(f"{name} is on {t.device}: the library runs on CUDA only "
+                               "(no CPU fallback)")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise ValueError("q, k, v must share a dtype")
+    if not (q.device == k.device == v.device):
+        raise ValueError("q, k, v must be on one device")
+    B, H, S, D = q.shape
+    if k.shape != (B, H, k.shape[2], D) or v.shape != k.shape:
+        raise ValueError(f"shape mismatch q{tuple(q.shape)} k{tuple(k.shape)} v{tuple(v.shape)}")
+    if D not in (64, 128):
+        raise ValueError(f"head_dim {D} unsupported (64 or 128)")
+    mask = mask.validate()
+    in_dtype = q.dtype
+    if in_dtype == torch.float32:
+        q, k, v = q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16)
+    elif in_dtype not in (torch.bfloat16, torch.float16):
+        raise ValueError(f"dtype {in_dtype} unsupported")
+    q, k, v = _prep(q), _prep(k), _prep(v)
+    dev = q.device
+    if out is None or in_dtype == torch.float32:
+        o = torch.empty(B, H, S, D, dtype=q.dtype, device=dev)
+    else:
+        if out.shape != q.shape or out.dtype != q.dtype or out.device != dev:
+            raise ValueError("out must match q in shape, dtype and device")
+        o = out
+        if o.stride(-1) != 1 or any(s % 8 for s in o.stride()[:-1]) or o.data_ptr() % 16:
+            raise ValueError("out must have unit last stride and 16-byte aligned rows")
+
+    hp = None
+    if mod in ("alibi", "temp"):
+        hp = (_cached_default(mod, H, dev) if head_param is None
+              else _param_tensor(head_param, H, dev))
+
+    p = N.AttnParams()
+    p.abi_version = N.ABI_VERSION
+    p.dtype = N.DTYPE_BF16 if q.dtype == torch.bfloat16 else N.DTYPE_F16
+    p.head_dim = D
+    p.norm = _NORMS[norm]
+    p.mod = _MODS[mod]
+    p.batch, p.heads, p.seqlen_q, p.seqlen_kv = B, H, S, k.shape[2]
+    p.q, p.k, p.v, p.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr()
+    for field, t in (("q_stride", q), ("k_stride", k), ("v_stride", v), ("o_stride", o)):
+        getattr(p, field)[:] = t.stride()[:3]
+    p.scale = (1.0 / math.sqrt(D)) if scale is None else float(scale)
+    p.softcap = float(softcap)
+    p.sig_bias = float(sig_bias)
+    p.out_scale = float(out_scale)
+    p.head_param = hp.data_ptr() if hp is not None else None
+    p.win_left, p.win_right = mask.left, mask.right
+    p.block, p.prefix, p.dilation = mask.block, mask.prefix, mask.dilation
+    p.status = _status_word(dev).data_ptr()
+
+    lib = N.load()
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        N.check(lib.chia_attn_fwd(ctypes.byref(p), ctypes.c_void_p(stream)),
+                f"chia_attn_fwd(norm={norm}, mod={mod}, mask={mask}, shape={tuple(q.shape)})")
+    return o.float() if in_dtype == torch.float32 else o
+
+
+# ---------------------------------------------------------------------------
+# the ten reference operators (extra_bench.py:51-62)
+# ---------------------------------------------------------------------------
+def softcap_gemma2(q, k, v, *, cap: float = 30.0, causal: bool = True,
+                   scale: Optional[float] = None):
+    """Gemma-2 softcap: ``softmax(cap*tanh(s/cap))`` (``extra_bench.py:60``)."""
+    return attention(q, k, v, mod="softcap", softcap=cap, mask=CAUSAL if causal else FULL,
+                     scale=scale)
+
+
+def bias_sliding_window(q, k, v, *, window: int = 256, scale: Optional[float] = None):
+    """Causal window ``(j<=i)&(i-j<window)`` (``extra_bench.py:61``)."""
+    if window < 1:
+        raise ValueError("window must be >= 1")
+    return attention(q, k, v, mask=Mask(left=window - 1, right=0), scale=scale)
+
+
+def bias_local(q, k, v, *, window: int = 256, scale: Optional[float] = None):
+    """Bidirectional band ``|i-j|<window`` (``extra_bench.py:57``)."""
+    if window < 1:
+        raise ValueError("window must be >= 1")
+    return attention(q, k, v, mask=Mask(left=window - 1, right=window - 1), scale=scale)
+
+
+def bias_alibi(q, k, v, *, slopes=None, scale: Optional[float] = None):
+    """ALiBi ``s + slope_h*(j-i)``, causal (``extra_bench.py:47-50``); default slopes h+1."""
+    return attention(q, k, v, mod="alibi", head_param=slopes, mask=CAUSAL, scale=scale)
+
+
+def bias_block_diagonal(q, k, v, *, block: int = 512, causal: bool = True,
+                        scale: Optional[float] = None):
+    """Same-block mask, causal inside blocks by default (``extra_bench.py:58``)."""
+    if block < 1:
+        raise ValueError("block must be >= 1")
+    return attention(q, k, v, mask=Mask(left=-1, right=0 if causal else -1, block=block),
+                     scale=scale)
+
+
+def bias_dilated(q, k, v, *, dilation: int = 4, scale: Optional[float] = None):
+    """``(j<=i)&((i-j)%dilation==0)`` (``extra_bench.py:56``)."""
+    if dilation < 1:
+        raise ValueError("dilation must be >= 1")
+    return attention(q, k, v, mask=Mask(left=-1, right=0, dilation=dilation), scale=scale)
+
+
+def bias_prefix_lm(q, k, v, *, prefix: int = 256, scale: Optional[float] = None):
+    """``(j<=i)|(j<prefix)`` (``extra_bench.py:59``)."""
+    if prefix < 0:
+        raise ValueError("prefix must be >= 0")
+    return attention(q, k, v, mask=Mask(left=-1, right=0, prefix=prefix), scale=scale)
+
+
+def temp_perhead(q, k, v, *, temps=None, scale: Optional[float] = None):
+    """``s*TEMP[h]``, causal (``extra_bench.py:35,54``); default TEMP ``0.5+h/H``.
+
+    ``temps`` multiplies the logits like the reference's TEMP; a temperature
+    tau dividing them is ``temps = 1/tau``.
+    """
+    return attention(q, k, v, mod="temp", head_param=temps, mask=CAUSAL, scale=scale)
+
+
+def sigmoid_attn(q, k, v, *, causal: bool = True, bias: float = 0.0,
+                 scale: Optional[float] = None):
+    """``sigmoid(s+bias)*mask @ v``, mask after the sigmoid (``sigmoid_fix.py:34-40``)."""
+    return attention(q, k, v, norm="sigmoid", sig_bias=bias, mask=CAUSAL if causal else FULL,
+                     scale=scale)
+
+
+def relu_attn(q, k, v, *, causal: bool = True, out_scale: float = 1.0,
+              scale: Optional[float] = None):
+    """``relu(s)*mask @ v * out_scale`` (``extra_bench.py:44``)."""
+    return attention(q, k, v, norm="relu", out_scale=out_scale,
+                     mask=CAUSAL if causal else FULL, scale=scale)
+
+
+OPS = {
+    "sigmoid_attn": sigmoid_attn,
+    "relu_attn": relu_attn,
+    "temp_perhead": temp_perhead,
+    "bias_alibi": bias_alibi,
+    "bias_dilated": bias_dilated,
+    "bias_local": bias_local,
+    "bias_block_diagonal": bias_block_diagonal,
+    "bias_prefix_lm": bias_prefix_lm,
+    "softcap_gemma2": softcap_gemma2,
+    "bias_sliding_window": bias_sliding_window,
+}
+
+
+def op_config(op: str, **kw) -> Mask:
+    """Mask of reference operator ``op`` with the given keyword overrides."""
+    if op in ("softcap_gemma2", "sigmoid_attn", "relu_attn"):
+        return CAUSAL if kw.get("causal", True) else FULL
+    if op in ("bias_alibi", "temp_perhead"):
+        return CAUSAL
+    if op == "bias_sliding_window":
+        w = kw.get("window", 256)
+        return Mask(left=w - 1, right=0)
+    if op == "bias_local":
+        w = kw.get("window", 256)
+        return Mask(left=w - 1, right=w - 1)
+    if op == "bias_block_diagonal":
+        return Mask(left=-1, right=0 if kw.get("causal", True) else -1,
+                    block=kw.get("block", 512))
+    if op == "bias_dilated":
+        return Mask(left=-1, right=0, dilation=kw.get("dilation", 4))
+    if op == "bias_prefix_lm":
+        return Mask(left=-1, right=0, prefix=kw.get("prefix", 256))
+    raise KeyError(op)
+
+
+def visible_pairs(mask: Mask, seqlen_q: int, seqlen_kv: Optional[int] = None) -> int:
+    """Visible (i, j) pairs of ``mask`` for one (batch, head) (host-side, no GPU)."""
+    p = N.AttnParams()
+    p.abi_version = N.ABI_VERSION
+    p.seqlen_q = seqlen_q
+    p.seqlen_kv = seqlen_q if seqlen_kv is None else seqlen_kv
+    p.win_left, p.win_right = mask.left, mask.right
+    p.block, p.prefix, p.dilation = mask.block, mask.prefix, mask.dilation
+    n = N.load().chia_attn_visible_pairs(ctypes.byref(p))
+    if n < 0:
+        raise ValueError(f"invalid mask {mask}")
+    return int(n)
+
+
+def tile_plan(mask: Mask, seqlen_q: int, row0: int, tile_m: int = 128, tile_n: int = 128,
+              seqlen_kv: Optional[int] = None):
+    """Key tiles ``(lo, hi, full_bits)`` the kernel visits for query rows ``[row0, row0+tile_m)``."""
+    p = N.AttnParams()
+    p.abi_version = N.ABI_VERSION
+    p.seqlen_q = seqlen_q
+    p.seqlen_kv = seqlen_q if seqlen_kv is None else seqlen_kv
+    p.win_left, p.win_right = mask.left, mask.right
+    p.block, p.prefix, p.dilation = mask.block, mask.prefix, mask.dilation
+    lo, hi, bits = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_uint64()
+    N.check(N.load().chia_attn_tile_plan(ctypes.byref(p), row0, tile_m, tile_n,
+                                         ctypes.byref(lo), ctypes.byref(hi), ctypes.byref(bits)))
+    return lo.value, hi.value, bits.value
+
+
+def mask_aware_flops(mask: Mask, B: int, H: int, S: int, D: int) -> int:
+    """``4 * D * visible_pairs * B * H`` -- the metric's FLOP count."""
+    return 4 * D * visible_pairs(mask, S) * B * H

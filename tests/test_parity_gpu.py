@@ -1,0 +1,237 @@
+"""GPU parity: the sm_100a kernel against the fp32 CPU oracle.
+
+Bar: max-abs <= 2e-2 and mean-abs <= 2e-3 against the
+fp32 eager reference for bf16/fp16 inputs. The reference's own acceptance
+gate, ``max|r-o| / max|r| < 3e-2`` (``synth10.py:15,182-184``), is checked
+as well, because outputs of some variants (ReLU/S, sigmoid - log S) are so
+small that absolute bounds alone would pass a wrong kernel.
+
+The absolute bounds assume O(1) outputs, which holds for every softmax
+variant and for the benchmark's sigmoid (bias -log S) and ReLU (scale 1/S).
+With the reference's default parameters sigmoid and ReLU are unnormalised
+and outputs grow like sqrt(S) (|o| ~ 30 at S=256): rounding the output to
+bf16 alone then costs |o| * 2^-9. The bounds are therefore multiplied by
+max(1, max|ref|) -- a no-op for O(1) outputs. The error there is the same
+bf16 rounding of P that the reference's own ``p.to(DT)`` performs.
+"""
+
+import math
+
+import pytest
+import torch
+
+import chia_proj_b200 as cp
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS, MEAN_ABS, REL_MAX = 2e-2, 2e-3, 3e-2
+
+
+def gen(B, H, S, D, dtype, seed=0, scale=1.0, Skv=None):
+    g = torch.Generator().manual_seed(seed)
+    shp = lambda s: (B, H, s, D)
+    q = (torch.randn(*shp(S), generator=g) * scale).to(dtype)
+    k = (torch.randn(*shp(Skv or S), generator=g) * scale).to(dtype)
+    v = (torch.randn(*shp(Skv or S), generator=g) * scale).to(dtype)
+    return q, k, v
+
+
+def check(out, ref, what=""):
+    out = out.float().cpu()
+    assert out.shape == ref.shape, what
+    assert torch.isfinite(out).all(), what
+    err = (out - ref).abs()
+    rmax = ref.abs().max().item()
+    rel = err.max().item() / (rmax + 1e-6)
+    tol_max = MAX_ABS * max(1.0, rmax)
+    tol_mean = MEAN_ABS * max(1.0, rmax)
+    assert err.max().item() <= tol_max, f"{what}: max-abs {err.max().item():.3e} > {tol_max:.3e}"
+    assert err.mean().item() <= tol_mean, f"{what}: mean-abs {err.mean().item():.3e}"
+    assert rel < REL_MAX, f"{what}: rel-max {rel:.3e}"
+
+
+def run(op, q, k, v, **kw):
+    dev = torch.device("cuda", 0)
+    out = cp.OPS[op](q.to(dev), k.to(dev), v.to(dev), **kw)
+    torch.cuda.synchronize()
+    return out
+
+
+@pytest.fixture(autouse=True)
+def _status_clean(cuda):
+    yield
+    cp.check_device_status(0)
+
+
+# ------------------------------------------------------------------ golden
+@pytest.mark.parametrize("op", sorted(cp.OPS))
+def test_golden_reference_vectors(cuda, golden, op):
+    """Outputs the reference's own eager code produced (tests/golden/)."""
+    out = run(op, golden["q"], golden["k"], golden["v"])
+    check(out, golden["outputs"][op], op)
+
+
+# ------------------------------------------------------- reference defaults
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("S", [1, 100, 129, 384, 1000])
+@pytest.mark.parametrize("op", sorted(cp.OPS))
+def test_reference_defaults(cuda, op, S, D, dtype):
+    q, k, v = gen(1, 2, S, D, dtype, seed=S + D)
+    ref = oracle.run_op(op, q, k, v)
+    check(run(op, q, k, v), ref, f"{op} S={S} D={D} {dtype}")
+
+
+@pytest.mark.parametrize("op", sorted(cp.OPS))
+def test_small_input_scale(cuda, op):
+    """The reference gate's second input scale, 0.01 (synth10.py:175-177)."""
+    q, k, v = gen(2, 2, 300, 128, torch.bfloat16, seed=7, scale=0.01)
+    ref = oracle.run_op(op, q, k, v)
+    out = run(op, q, k, v).float().cpu()
+    err = (out - ref).abs().max().item()
+    assert err / (ref.abs().max().item() + 1e-6) < REL_MAX, op
+
+
+# ---------------------------------------------------- benchmark parameters
+def _tau(H, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return 0.5 + 1.5 * torch.rand(H, generator=g)
+
+
+BASELINE_CASES = [
+    # (op, kwargs, oracle kwargs, B, H, S, D, dtype)
+    ("softcap_gemma2", dict(cap=50.0, causal=False), dict(cap=50.0, causal=False),
+     1, 2, 512, 64, torch.bfloat16),
+    ("bias_sliding_window", dict(window=256), dict(window=256), 1, 2, 2048, 64, torch.bfloat16),
+    ("bias_alibi", dict(slopes=cp.alibi_slopes_geometric(4)),
+     dict(slopes=cp.alibi_slopes_geometric(4)), 1, 4, 1024, 128, torch.float16),
+    ("temp_perhead", dict(temps=1.0 / _tau(4)), dict(temps=1.0 / _tau(4)),
+     1, 4, 1024, 128, torch.float16),
+    ("bias_prefix_lm", dict(prefix=1024), dict(prefix=1024), 1, 2, 1500, 128, torch.bfloat16),
+    ("bias_block_diagonal", dict(block=256), dict(block=256), 1, 2, 1024, 128, torch.bfloat16),
+    ("bias_block_diagonal", dict(block=256, causal=False), dict(block=256, causal=False),
+     1, 2, 1024, 128, torch.bfloat16),
+    ("bias_dilated", dict(dilation=4), dict(dilation=4), 1, 2, 1024, 128, torch.bfloat16),
+    ("bias_dilated", dict(dilation=4), dict(dilation=4), 1, 2, 1023, 128, torch.bfloat16),
+    ("bias_dilated", dict(dilation=3), dict(dilation=3), 2, 1, 999, 64, torch.bfloat16),
+    ("sigmoid_attn", dict(causal=False, bias=-math.log(2048)),
+     dict(causal=False, bias=-math.log(2048)), 1, 2, 2048, 128, torch.bfloat16),
+    ("relu_attn", dict(causal=False, out_scale=1.0 / 2048), dict(causal=False, out_scale=1.0 / 2048),
+     1, 2, 2048, 128, torch.bfloat16),
+    ("bias_local", dict(window=100), dict(window=100), 1, 2, 700, 64, torch.bfloat16),
+    ("bias_block_diagonal", dict(block=100), dict(block=100), 1, 2, 700, 64, torch.float16),
+    ("bias_prefix_lm", dict(prefix=200), dict(prefix=200), 1, 2, 700, 64, torch.bfloat16),
+    ("bias_sliding_window", dict(window=1), dict(window=1), 1, 2, 300, 64, torch.bfloat16),
+]
+
+
+@pytest.mark.parametrize("case", BASELINE_CASES,
+                         ids=[f"{c[0]}-{i}" for i, c in enumerate(BASELINE_CASES)])
+def test_benchmark_parameters(cuda, case):
+    op, kw, okw, B, H, S, D, dtype = case
+    q, k, v = gen(B, H, S, D, dtype, seed=S)
+    ref = oracle.run_op(op, q, k, v, **okw)
+    check(run(op, q, k, v, **kw), ref, f"{op} {kw}")
+
+
+# ------------------------------------------------------------------ layouts
+def test_strided_inputs(cuda):
+    """[B, S, H, D] storage viewed as [B, H, S, D] (non-contiguous, TMA strides)."""
+    B, H, S, D = 2, 3, 333, 128
+    g = torch.Generator().manual_seed(3)
+    base = [torch.randn(B, S, H, D, generator=g).to(torch.bfloat16) for _ in range(3)]
+    q, k, v = (t.transpose(1, 2) for t in base)
+    ref = oracle.run_op("softcap_gemma2", q, k, v)
+    dev = torch.device("cuda", 0)
+    qd, kd, vd = (t.to(dev).transpose(1, 2) for t in base)
+    assert not qd.is_contiguous()
+    check(cp.softcap_gemma2(qd, kd, vd), ref, "strided")
+
+
+def test_fp32_inputs_accepted(cuda):
+    """Config-1 shape in fp32 (computed in bf16 on the tensor cores)."""
+    q, k, v = gen(1, 8, 512, 64, torch.float32, seed=1)
+    ref = oracle.run_op("softcap_gemma2", q, k, v, cap=50.0, causal=False)
+    out = run("softcap_gemma2", q, k, v, cap=50.0, causal=False)
+    assert out.dtype == torch.float32
+    check(out, ref, "fp32 config 1")
+
+
+def test_preallocated_output(cuda):
+    q, k, v = gen(1, 2, 256, 64, torch.bfloat16, seed=2)
+    dev = torch.device("cuda", 0)
+    out = torch.full((1, 2, 256, 64), float("nan"), dtype=torch.bfloat16, device=dev)
+    r = cp.attention(q.to(dev), k.to(dev), v.to(dev), out=out)
+    assert r.data_ptr() == out.data_ptr()
+    check(out, oracle.run_op("bias_dilated", q, k, v, dilation=1), "out=")
+
+
+# ------------------------------------------- full-size, size-independent checks
+def test_linearity_in_v_is_exact(cuda):
+    q, k, v = gen(1, 4, 2048, 128, torch.bfloat16, seed=11)
+    dev = torch.device("cuda", 0)
+    q, k, v = q.to(dev), k.to(dev), v.to(dev)
+    for op in cp.OPS:
+        a = cp.OPS[op](q, k, v)
+        b = cp.OPS[op](q, k, v * 2)
+        assert torch.equal(a * 2, b), op
+
+
+@pytest.mark.parametrize("op,kw", [
+    ("bias_sliding_window", {}), ("bias_block_diagonal", dict(block=256)),
+    ("bias_prefix_lm", dict(prefix=1024)), ("bias_dilated", {}), ("softcap_gemma2", {}),
+    ("bias_local", {}),
+])
+def test_invisible_keys_do_not_matter_at_headline_shape(cuda, op, kw):
+    """B4 H16 S4096 D128: perturbing keys/values a mask hides leaves the output
+    bit-identical; two sampled heads also match the oracle."""
+    B, H, S, D = 4, 16, 4096, 128
+    dev = torch.device("cuda", 0)
+    q, k, v = (t.to(dev) for t in gen(B, H, S, D, torch.bfloat16, seed=5))
+    out = cp.OPS[op](q, k, v, **kw)
+    # perturb keys/values of query rows [3000, 3100) that are invisible to all of them
+    mask = cp.op_config(op, **kw)
+    i = torch.arange(3000, 3100).view(-1, 1)
+    j = torch.arange(S).view(1, -1)
+    vis = torch.zeros(100, S, dtype=torch.bool)
+    band = torch.ones_like(vis)
+    if mask.left >= 0:
+        band &= (i - j) <= mask.left
+    if mask.right >= 0:
+        band &= (j - i) <= mask.right
+    if mask.block > 0:
+        band &= (i // mask.block) == (j // mask.block)
+    band &= ((i - j) % mask.dilation) == 0
+    vis = band | (j < mask.prefix)
+    hidden = (~vis.any(0)).nonzero().flatten().to(dev)
+    k2, v2 = k.clone(), v.clone()
+    k2[:, :, hidden] = torch.randn_like(k2[:, :, hidden]) * 3
+    v2[:, :, hidden] = torch.randn_like(v2[:, :, hidden]) * 3
+    out2 = cp.OPS[op](q, k2, v2, **kw)
+    assert torch.equal(out[:, :, 3000:3100], out2[:, :, 3000:3100])
+    for (b, h) in ((0, 0), (3, 15)):
+        ref = oracle.run_op(op, q[b:b + 1, h:h + 1].cpu(), k[b:b + 1, h:h + 1].cpu(),
+                            v[b:b + 1, h:h + 1].cpu(), **kw)
+        check(out[b:b + 1, h:h + 1], ref, f"{op} head ({b},{h})")
+
+
+@pytest.mark.parametrize("op", ["sigmoid_attn", "relu_attn"])
+def test_config5_heads_match_oracle(cuda, op):
+    """Config 5 shape per head (S=8192, D=128, non-causal): sampled heads."""
+    S = 8192
+    kw = dict(causal=False, bias=-math.log(S)) if op == "sigmoid_attn" else \
+        dict(causal=False, out_scale=1.0 / S)
+    q, k, v = gen(1, 3, S, 128, torch.bfloat16, seed=9)
+    out = run(op, q, k, v, **kw)
+    ref = oracle.run_op(op, q[:, :2], k[:, :2], v[:, :2], **kw)
+    check(out[:, :2], ref, op)
+
+
+def test_repeat_calls_are_deterministic(cuda):
+    q, k, v = gen(2, 4, 1000, 128, torch.bfloat16, seed=4)
+    dev = torch.device("cuda", 0)
+    q, k, v = q.to(dev), k.to(dev), v.to(dev)
+    a = cp.bias_alibi(q, k, v, slopes=cp.alibi_slopes_geometric(4))
+    for _ in range(3):
+        assert torch.equal(a, cp.bias_alibi(q, k, v, slopes=cp.alibi_slopes_geometric(4)))
