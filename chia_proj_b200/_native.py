@@ -14,7 +14,8 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "_lib", "libchia_attn.so")
 
-ABI_VERSION = 1
+ABI_VERSION = 2
+WORKSPACE_BYTES = 256
 
 DTYPE_BF16, DTYPE_F16 = 0, 1
 NORM_SOFTMAX, NORM_SIGMOID, NORM_RELU = 0, 1, 2
@@ -72,6 +73,7 @@ class AttnParams(ctypes.Structure):
         ("prefix", ctypes.c_int64),
         ("dilation", ctypes.c_int64),
         ("status", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p),
     ]
 
 

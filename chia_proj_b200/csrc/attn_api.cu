@@ -98,6 +98,7 @@ int validate(const chia_attn_params_t *p) {
     return CHIA_ERR_INVALID_ARGUMENT;
   if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->o))
     return CHIA_ERR_MISALIGNED;
+  if ((reinterpret_cast<uintptr_t>(p->workspace) & 15u) != 0) return CHIA_ERR_MISALIGNED;
   const int64_t *strides[4] = {p->q_stride, p->k_stride, p->v_stride, p->o_stride};
   for (auto *s : strides)
     for (int d = 0; d < 3; ++d) {
@@ -268,13 +269,20 @@ int chia_attn_fwd(const chia_attn_params_t *p, void *stream) {
   a.mask = g;
   a.heads = static_cast<int32_t>(p->heads);
   a.vdil = dv.vdil;
-  const int64_t rows_per_cta = 2 * 128;
-  const int64_t nqb = (g.sq + rows_per_cta - 1) / rows_per_cta;
+  const int64_t rows_per_unit = 2 * 128;
+  const int64_t nqb = (g.sq + rows_per_unit - 1) / rows_per_unit;
   const int64_t nvh = p->batch * p->heads * dv.vdil;
-  const int64_t nblocks = nqb * nvh;
-  if (nblocks > 0x7fffffffLL || nqb > 0x7fffffffLL) return CHIA_ERR_UNSUPPORTED;
+  const int64_t nunits = nqb * nvh;
+  if (nunits > 0x7fffffffLL) return CHIA_ERR_UNSUPPORTED;
   a.n_qblocks = static_cast<int32_t>(nqb);
   a.n_vheads = static_cast<int32_t>(nvh);
+  a.n_units = static_cast<int32_t>(nunits);
+  a.sched = static_cast<int32_t *>(p->workspace);
+  // persistent grid: one CTA per SM (shared memory admits no more)
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
+    return CHIA_ERR_NO_DEVICE;
+  const int64_t nblocks = nunits < sms ? nunits : sms;
   a.score_scale = p->scale;
   a.softcap = p->softcap;
   a.sig_bias = p->sig_bias;

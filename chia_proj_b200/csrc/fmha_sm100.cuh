@@ -57,6 +57,8 @@ struct KernelArgs {
   int32_t vdil;         // rows of one virtual head are i' * vdil + r (1 = plain)
   int32_t n_qblocks;    // ceil(sq / (NQ * BM))
   int32_t n_vheads;     // B * H * vdil
+  int32_t n_units;      // n_qblocks * n_vheads work units
+  int32_t *sched;       // [next unit, finished CTAs] or null (static round robin)
   float score_scale;    // multiplies q.k before the mod (1/sqrt(D) by default)
   float softcap;        // KIND_SOFTCAP
   float sig_bias;       // KIND_SIGMOID
@@ -83,18 +85,24 @@ struct FmhaConfig {
   static constexpr int OFF_K = OFF_Q + NQ * Q_TILE_BYTES;
   static constexpr int OFF_V = OFF_K + NS * KV_TILE_BYTES;
   static constexpr int OFF_BAR = OFF_V + NS * KV_TILE_BYTES;
-  // barriers: q | k_full[NS] k_empty[NS] v_full[NS] v_empty[NS] | s_full[2] p_full[2] o_full[2] | drain
+  // barriers: q q_empty | k_full[NS] k_empty[NS] v_full[NS] v_empty[NS] |
+  //           s_full[2] p_full[2] o_full[2] o_empty[2] | unit_full[2] unit_empty[2] | drain
   static constexpr int BAR_Q = 0;
-  static constexpr int BAR_KFULL = 1;
+  static constexpr int BAR_QEMPTY = 1;
+  static constexpr int BAR_KFULL = 2;
   static constexpr int BAR_KEMPTY = BAR_KFULL + NS;
   static constexpr int BAR_VFULL = BAR_KEMPTY + NS;
   static constexpr int BAR_VEMPTY = BAR_VFULL + NS;
   static constexpr int BAR_SFULL = BAR_VEMPTY + NS;
   static constexpr int BAR_PFULL = BAR_SFULL + NQ;
   static constexpr int BAR_OFULL = BAR_PFULL + NQ;
-  static constexpr int BAR_DRAIN = BAR_OFULL + NQ;
+  static constexpr int BAR_OEMPTY = BAR_OFULL + NQ;
+  static constexpr int BAR_UFULL = BAR_OEMPTY + NQ;
+  static constexpr int BAR_UEMPTY = BAR_UFULL + 2;
+  static constexpr int BAR_DRAIN = BAR_UEMPTY + 2;
   static constexpr int NUM_BARS = BAR_DRAIN + 1;
-  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // tmem base, abort flag
+  // misc: [0] TMEM base, [1] abort flag, [2..3] unit ring
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 16;
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack for 1024-byte alignment
   // 12 warps: warpgroups 0 and 1 = softmax (one query tile each), warpgroup 2
@@ -104,8 +112,8 @@ struct FmhaConfig {
   static constexpr int THREADS = 384;
   static constexpr int MMA_WARP = 8;
   static constexpr int LOAD_WARP = 9;
-  static constexpr int REG_SOFTMAX = 224;
-  static constexpr int REG_OTHER = 56;
+  static constexpr int REG_SOFTMAX = 216;
+  static constexpr int REG_OTHER = 72;
   static_assert(2 * 128 * REG_SOFTMAX + 128 * REG_OTHER == THREADS * 168, "register split");
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t TMEM_S = 0;    // + w * 128
@@ -281,6 +289,47 @@ __device__ __forceinline__ void store_rows(uint32_t tO, float inv, bool row_ok, 
   }
 }
 
+// One work unit: two query tiles (NQ * BM rows) of one (virtual) head.
+struct UnitInfo {
+  int r_res, h, b;
+  int64_t m0;
+  int64_t tlo[2], thi[2];  // key-tile range per query tile (empty: lo == hi)
+  int64_t jlo, jhi;        // union of both ranges
+  __device__ __forceinline__ bool active(int w, int64_t j) const {
+    return j >= tlo[w] && j < thi[w];
+  }
+  __device__ __forceinline__ bool any_active(int64_t j) const { return active(0, j) || active(1, j); }
+  __device__ __forceinline__ bool wg_on(int w) const { return tlo[w] < thi[w]; }
+};
+
+// Units are ordered head-major with the heaviest query block of a head first,
+// so the units in flight at any time share K/V in L2 and the light blocks
+// finish the schedule.
+template <int BM, int BN>
+__device__ __forceinline__ void decode_unit(int u, const KernelArgs &a, UnitInfo &U) {
+  const int vh = u / a.n_qblocks;
+  const int qb = a.n_qblocks - 1 - (u % a.n_qblocks);
+  U.r_res = vh % a.vdil;
+  U.h = (vh / a.vdil) % a.heads;
+  U.b = vh / (a.vdil * a.heads);
+  U.m0 = static_cast<int64_t>(qb) * (2 * BM);
+  U.jlo = INT64_MAX;
+  U.jhi = 0;
+#pragma unroll
+  for (int w = 0; w < 2; ++w) {
+    tile_range(a.mask, U.m0 + w * BM, U.m0 + w * BM + BM - 1, BN, U.tlo[w], U.thi[w]);
+    if (U.tlo[w] < U.thi[w]) {
+      U.jlo = imin64(U.jlo, U.tlo[w]);
+      U.jhi = imax64(U.jhi, U.thi[w]);
+    }
+  }
+}
+
+// Persistent kernel: each CTA loops over work units. With a scheduler
+// workspace the load warp takes the next unit from a global counter (dynamic
+// balance; the last CTA to finish puts the counter back to zero), otherwise
+// CTA c runs units c, c + grid, c + 2 grid, ... . The unit index travels to the
+// other roles through a two-slot ring in shared memory.
 template <int D, bool BF16, int KIND>
 __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
     fmha_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -298,42 +347,16 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
   auto bar = [&](int idx) -> uint32_t { return sbase + C::OFF_BAR + idx * 8; };
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::OFF_MISC);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::OFF_MISC + 4);
+  volatile int *unit_ring = reinterpret_cast<volatile int *>(smem + C::OFF_MISC + 8);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
-  // ---- work unit: heavy query blocks of a head first, heads in order ----
-  const int cta = blockIdx.x;
-  const int vh = cta / args.n_qblocks;
-  const int qb = args.n_qblocks - 1 - (cta % args.n_qblocks);
-  const int r_res = vh % args.vdil;  // residue class (dilated fast path)
-  const int h = (vh / args.vdil) % args.heads;
-  const int b = vh / (args.vdil * args.heads);
-  const int64_t m0 = static_cast<int64_t>(qb) * (NQ * BM);
   const MaskGeom &g = args.mask;
-
-  // key-tile range of each query tile (identical in every role)
-  int64_t tlo[NQ], thi[NQ];
-#pragma unroll
-  for (int w = 0; w < NQ; ++w) tile_range(g, m0 + w * BM, m0 + w * BM + BM - 1, BN, tlo[w], thi[w]);
-  int64_t jlo = INT64_MAX, jhi = 0;
-#pragma unroll
-  for (int w = 0; w < NQ; ++w)
-    if (tlo[w] < thi[w]) {
-      jlo = imin64(jlo, tlo[w]);
-      jhi = imax64(jhi, thi[w]);
-    }
-  auto active = [&](int w, int64_t j) { return j >= tlo[w] && j < thi[w]; };
-  auto any_active = [&](int64_t j) {
-    bool a = false;
-#pragma unroll
-    for (int w = 0; w < NQ; ++w) a |= active(w, j);
-    return a;
-  };
 
   // ---- setup: barriers, TMEM ----
   if (threadIdx.x == 0) {
     ptx::mbar_init(bar(C::BAR_Q), 1);
+    ptx::mbar_init(bar(C::BAR_QEMPTY), 1);
     for (int s = 0; s < NS; ++s) {
       ptx::mbar_init(bar(C::BAR_KFULL + s), 1);
       ptx::mbar_init(bar(C::BAR_KEMPTY + s), 1);
@@ -342,8 +365,13 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
     }
     for (int w = 0; w < NQ; ++w) {
       ptx::mbar_init(bar(C::BAR_SFULL + w), 1);
-      ptx::mbar_init(bar(C::BAR_PFULL + w), 4);  // one arrive per softmax warp
+      ptx::mbar_init(bar(C::BAR_PFULL + w), 4);   // one arrive per softmax warp
       ptx::mbar_init(bar(C::BAR_OFULL + w), 1);
+      ptx::mbar_init(bar(C::BAR_OEMPTY + w), 4);  // one arrive per softmax warp
+    }
+    for (int s = 0; s < 2; ++s) {
+      ptx::mbar_init(bar(C::BAR_UFULL + s), 1);
+      ptx::mbar_init(bar(C::BAR_UEMPTY + s), 1 + 8);  // MMA thread + 8 softmax warps
     }
     ptx::mbar_init(bar(C::BAR_DRAIN), 1);
     *abort_flag = 0;
@@ -366,58 +394,72 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
   const WaitCtx wc{abort_flag, args.status, args.timeout_ns};
 
   if (warp >= 8) {
-   ptx::setmaxnreg_dec<C::REG_OTHER>();
-   if (warp == C::LOAD_WARP) {
-    // =========================== TMA producer ===========================
-    if (lane == 0) {
-      uint32_t qbytes = 0;
-#pragma unroll
-      for (int w = 0; w < NQ; ++w)
-        if (tlo[w] < thi[w]) qbytes += C::Q_TILE_BYTES;
-      ptx::mbar_arrive_expect_tx(bar(C::BAR_Q), qbytes);
-#pragma unroll
-      for (int w = 0; w < NQ; ++w)
-        if (tlo[w] < thi[w])
-#pragma unroll
-          for (int c = 0; c < C::NCHUNK; ++c)
-            ptx::tma_load_5d(sbase + C::OFF_Q + w * C::Q_TILE_BYTES + c * C::CHUNK_Q_BYTES, &tm_q,
-                             bar(C::BAR_Q), c * 64, static_cast<int>(m0 + w * BM), r_res, h, b);
+    ptx::setmaxnreg_dec<C::REG_OTHER>();
+    if (warp == C::LOAD_WARP && lane == 0) {
+      // ==================== scheduler + TMA producer ====================
       uint32_t it = 0;
       int64_t last_use[2 * NS];
       for (int s = 0; s < 2 * NS; ++s) last_use[s] = -1;
-      for (int64_t j = jlo; j < jhi; ++j) {
-        if (!any_active(j)) continue;
-        const int s = it % NS;
-        const uint32_t ph = (it / NS) & 1;
-        if (!bounded_wait(wc, bar(C::BAR_KEMPTY + s), ph ^ 1)) break;
-        ptx::mbar_arrive_expect_tx(bar(C::BAR_KFULL + s), C::KV_TILE_BYTES);
+      for (int k = 0;; ++k) {
+        const int slot = k & 1;
+        if (!bounded_wait(wc, bar(C::BAR_UEMPTY + slot), ((k >> 1) & 1) ^ 1)) break;
+        int u = args.sched ? atomicAdd(args.sched, 1) : static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
+        if (u >= args.n_units || u < 0) u = -1;
+        unit_ring[slot] = u;
+        ptx::mbar_arrive(bar(C::BAR_UFULL + slot));
+        if (u < 0) break;
+        UnitInfo U;
+        decode_unit<BM, BN>(u, args, U);
+        // Q tiles: the previous unit's S MMAs must be done with the buffer
+        if (k > 0 && !bounded_wait(wc, bar(C::BAR_QEMPTY), (k - 1) & 1)) break;
+        uint32_t qbytes = 0;
 #pragma unroll
-        for (int c = 0; c < C::NCHUNK; ++c)
-          ptx::tma_load_5d(sbase + C::OFF_K + s * C::KV_TILE_BYTES + c * C::CHUNK_KV_BYTES, &tm_k,
-                           bar(C::BAR_KFULL + s), c * 64, static_cast<int>(j * BN), r_res, h, b);
-        last_use[s] = it;
-        if (!bounded_wait(wc, bar(C::BAR_VEMPTY + s), ph ^ 1)) break;
-        ptx::mbar_arrive_expect_tx(bar(C::BAR_VFULL + s), C::KV_TILE_BYTES);
+        for (int w = 0; w < NQ; ++w)
+          if (U.wg_on(w)) qbytes += C::Q_TILE_BYTES;
+        ptx::mbar_arrive_expect_tx(bar(C::BAR_Q), qbytes);
 #pragma unroll
-        for (int c = 0; c < C::NCHUNK; ++c)
-          ptx::tma_load_5d(sbase + C::OFF_V + s * C::KV_TILE_BYTES + c * C::CHUNK_KV_BYTES, &tm_v,
-                           bar(C::BAR_VFULL + s), c * 64, static_cast<int>(j * BN), r_res, h, b);
-        last_use[NS + s] = it;
-        ++it;
+        for (int w = 0; w < NQ; ++w)
+          if (U.wg_on(w))
+#pragma unroll
+            for (int c = 0; c < C::NCHUNK; ++c)
+              ptx::tma_load_5d(sbase + C::OFF_Q + w * C::Q_TILE_BYTES + c * C::CHUNK_Q_BYTES,
+                               &tm_q, bar(C::BAR_Q), c * 64, static_cast<int>(U.m0 + w * BM),
+                               U.r_res, U.h, U.b);
+        bool ok = true;
+        for (int64_t j = U.jlo; j < U.jhi; ++j) {
+          if (!U.any_active(j)) continue;
+          const int s = it % NS;
+          const uint32_t ph = (it / NS) & 1;
+          if (!bounded_wait(wc, bar(C::BAR_KEMPTY + s), ph ^ 1)) { ok = false; break; }
+          ptx::mbar_arrive_expect_tx(bar(C::BAR_KFULL + s), C::KV_TILE_BYTES);
+#pragma unroll
+          for (int c = 0; c < C::NCHUNK; ++c)
+            ptx::tma_load_5d(sbase + C::OFF_K + s * C::KV_TILE_BYTES + c * C::CHUNK_KV_BYTES,
+                             &tm_k, bar(C::BAR_KFULL + s), c * 64, static_cast<int>(j * BN),
+                             U.r_res, U.h, U.b);
+          last_use[s] = it;
+          if (!bounded_wait(wc, bar(C::BAR_VEMPTY + s), ph ^ 1)) { ok = false; break; }
+          ptx::mbar_arrive_expect_tx(bar(C::BAR_VFULL + s), C::KV_TILE_BYTES);
+#pragma unroll
+          for (int c = 0; c < C::NCHUNK; ++c)
+            ptx::tma_load_5d(sbase + C::OFF_V + s * C::KV_TILE_BYTES + c * C::CHUNK_KV_BYTES,
+                             &tm_v, bar(C::BAR_VFULL + s), c * 64, static_cast<int>(j * BN),
+                             U.r_res, U.h, U.b);
+          last_use[NS + s] = it;
+          ++it;
+        }
+        if (!ok) break;
       }
-      // Drain: every copy this thread issued must land before the CTA exits.
-      // In a normal run these phases have completed already.
+      // Drain: every copy this thread issued lands before the CTA exits (the
+      // Q copies complete before the MMA thread can finish its last unit).
       for (int s = 0; s < NS; ++s) {
         if (last_use[s] >= 0)
           bounded_wait(wc, bar(C::BAR_KFULL + s), (last_use[s] / NS) & 1, false);
         if (last_use[NS + s] >= 0)
           bounded_wait(wc, bar(C::BAR_VFULL + s), (last_use[NS + s] / NS) & 1, false);
       }
-    }
-    __syncwarp();
-  } else if (warp == C::MMA_WARP) {
-    // =========================== UMMA issuer ===========================
-    if (lane == 0) {
+    } else if (warp == C::MMA_WARP && lane == 0) {
+      // =========================== UMMA issuer ===========================
       constexpr uint32_t IDESC_QK = ptx::make_idesc_f16(BM, BN, BF16, false, false);
       constexpr uint32_t IDESC_PV = ptx::make_idesc_f16(BM, D, BF16, false, true);
       const uint32_t q_s = sbase + C::OFF_Q, k_s = sbase + C::OFF_K, v_s = sbase + C::OFF_V;
@@ -444,51 +486,55 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
         }
       };
 
-      bool ok = (jlo < jhi) && bounded_wait(wc, bar(C::BAR_Q), 0);
-      uint32_t kit = 0, vit = 0, pcnt[NQ];
-      bool first[NQ];
-#pragma unroll
-      for (int w = 0; w < NQ; ++w) {
-        pcnt[w] = 0;
-        first[w] = true;
-      }
-      if (ok) {
-        ptx::tc_fence_after();
-        ok = bounded_wait(wc, bar(C::BAR_KFULL + 0), 0);
-      }
-      if (ok) {
+      uint32_t kit = 0, vit = 0, pcnt[NQ] = {0, 0}, units_w[NQ] = {0, 0};
+      bool ok = true;
+      for (int k = 0; ok; ++k) {
+        const int slot = k & 1;
+        if (!bounded_wait(wc, bar(C::BAR_UFULL + slot), (k >> 1) & 1)) break;
+        const int u = unit_ring[slot];
+        ptx::mbar_arrive(bar(C::BAR_UEMPTY + slot));
+        if (u < 0) break;
+        UnitInfo U;
+        decode_unit<BM, BN>(u, args, U);
+        if (!bounded_wait(wc, bar(C::BAR_Q), k & 1)) break;
+        if (!bounded_wait(wc, bar(C::BAR_KFULL + kit % NS), (kit / NS) & 1)) break;
         ptx::tc_fence_after();
 #pragma unroll
         for (int w = 0; w < NQ; ++w)
-          if (active(w, jlo)) {
-            issue_s(w, 0);
+          if (U.active(w, U.jlo)) {
+            issue_s(w, kit % NS);
             ptx::umma_commit(bar(C::BAR_SFULL + w));
           }
-        ptx::umma_commit(bar(C::BAR_KEMPTY + 0));
-        kit = 1;
-        for (int64_t j = jlo; ok && j < jhi;) {
+        ptx::umma_commit(bar(C::BAR_KEMPTY + kit % NS));
+        ++kit;
+        bool first[NQ] = {true, true};
+        for (int64_t j = U.jlo; j < U.jhi;) {
           int64_t jn = j + 1;
-          while (jn < jhi && !any_active(jn)) ++jn;
-          const bool has_next = jn < jhi;
+          while (jn < U.jhi && !U.any_active(jn)) ++jn;
+          const bool has_next = jn < U.jhi;
+          if (!has_next) ptx::umma_commit(bar(C::BAR_QEMPTY));  // every S of this unit issued
           const int vs = vit % NS;
           const int ks = kit % NS;
-          if (!bounded_wait(wc, bar(C::BAR_VFULL + vs), (vit / NS) & 1)) break;
-          if (has_next && !bounded_wait(wc, bar(C::BAR_KFULL + ks), (kit / NS) & 1)) break;
+          if (!bounded_wait(wc, bar(C::BAR_VFULL + vs), (vit / NS) & 1)) { ok = false; break; }
+          if (has_next && !bounded_wait(wc, bar(C::BAR_KFULL + ks), (kit / NS) & 1)) { ok = false; break; }
           ptx::tc_fence_after();
 #pragma unroll
           for (int w = 0; w < NQ; ++w) {
-            if (active(w, j)) {
-              if (!bounded_wait(wc, bar(C::BAR_PFULL + w), pcnt[w] & 1)) {
-                ok = false;
-                break;
-              }
+            if (U.active(w, j)) {
+              if (!bounded_wait(wc, bar(C::BAR_PFULL + w), pcnt[w] & 1)) { ok = false; break; }
               ++pcnt[w];
+              // the previous unit's epilogue must have read O_w before it is overwritten
+              if (first[w] && units_w[w] > 0 &&
+                  !bounded_wait(wc, bar(C::BAR_OEMPTY + w), (units_w[w] - 1) & 1)) { ok = false; break; }
               ptx::tc_fence_after();
               issue_pv(w, vs, first[w]);
               first[w] = false;
-              if (j == thi[w] - 1) ptx::umma_commit(bar(C::BAR_OFULL + w));
+              if (j == U.thi[w] - 1) {
+                ptx::umma_commit(bar(C::BAR_OFULL + w));
+                ++units_w[w];
+              }
             }
-            if (has_next && active(w, jn)) {
+            if (has_next && U.active(w, jn)) {
               issue_s(w, ks);
               ptx::umma_commit(bar(C::BAR_SFULL + w));
             }
@@ -508,54 +554,61 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
       bounded_wait(wc, bar(C::BAR_DRAIN), 0, false);
     }
     __syncwarp();
-   }
   } else {
     ptx::setmaxnreg_inc<C::REG_SOFTMAX>();
     // ======================= softmax / epilogue =======================
     const int w = warp >> 2;           // query tile of this warpgroup
     const int quad = warp & 3;         // TMEM lane quadrant of this warp
     const int row = quad * 32 + lane;  // row inside the query tile
-    const int i = static_cast<int>(m0) + w * BM + row;
-    const int64_t r0 = m0 + w * BM, r1 = r0 + BM - 1;
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t tS = tmem_base + lane_off + C::TMEM_S + w * 128;
     const uint32_t tO = tmem_base + lane_off + C::TMEM_O + w * 128;
+    const int prefix = static_cast<int>(g.prefix);
+    const int dil = static_cast<int>(g.dil);
+    const float score_scale = args.score_scale;
 
-    if (tlo[w] < thi[w]) {
+    uint32_t cnt = 0, units_w = 0;
+    for (int k = 0;; ++k) {
+      const int slot = k & 1;
+      if (!bounded_wait(wc, bar(C::BAR_UFULL + slot), (k >> 1) & 1)) break;
+      const int u = unit_ring[slot];
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar(C::BAR_UEMPTY + slot));
+      if (u < 0) break;
+      UnitInfo U;
+      decode_unit<BM, BN>(u, args, U);
+      if (!U.wg_on(w)) continue;
+
+      const int i = static_cast<int>(U.m0) + w * BM + row;
+      const int64_t r0 = U.m0 + w * BM, r1 = r0 + BM - 1;
       int64_t blo64, bhi64;
       row_band(g, i, blo64, bhi64);
       const bool band_empty = bhi64 < blo64;
       const int blo = band_empty ? (1 << 30) : static_cast<int>(blo64);
       const uint32_t span = band_empty ? 0u : static_cast<uint32_t>(bhi64 - blo64);
-      const int prefix = static_cast<int>(g.prefix);
-      const int dil = static_cast<int>(g.dil);
       // per-kind constants (log2 domain for the softmax kinds)
       float hp = 1.0f;
-      if (args.head_param != nullptr) hp = args.head_param[h];
+      if (args.head_param != nullptr) hp = args.head_param[U.h];
       EpiConsts kc;
-      kc.k_mul = args.score_scale * LOG2E;
+      kc.k_mul = score_scale * LOG2E;
       kc.k_cap = 0.f;
       kc.k_bias = 0.f;
       if (KIND == KIND_SOFTMAX) kc.k_mul *= hp;
       if (KIND == KIND_SOFTCAP) {
-        kc.k_mul = args.score_scale / args.softcap;
+        kc.k_mul = score_scale / args.softcap;
         kc.k_cap = args.softcap * LOG2E;
       }
       if (KIND == KIND_ALIBI) kc.k_bias = hp * LOG2E * static_cast<float>(args.vdil);
       if (KIND == KIND_SIGMOID) {
-        kc.k_mul = -args.score_scale * LOG2E;
+        kc.k_mul = -score_scale * LOG2E;
         kc.k_bias = -args.sig_bias * LOG2E;
       }
-      if (KIND == KIND_RELU) kc.k_mul = args.score_scale;
+      if (KIND == KIND_RELU) kc.k_mul = score_scale;
 
       float m_run = -INFINITY, l_run = 0.f;
-      uint32_t cnt = 0;
       bool ok = true;
-      for (int64_t t = tlo[w]; t < thi[w]; ++t, ++cnt) {
-        if (!bounded_wait(wc, bar(C::BAR_SFULL + w), cnt & 1)) {
-          ok = false;
-          break;
-        }
+      for (int64_t t = U.tlo[w]; t < U.thi[w]; ++t, ++cnt) {
+        if (!bounded_wait(wc, bar(C::BAR_SFULL + w), cnt & 1)) { ok = false; break; }
         ptx::tc_fence_after();
         uint32_t sr[4][32];
 #pragma unroll
@@ -589,7 +642,7 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
             l_run *= alpha;
             m_run = m_new;
           }
-          if (cnt > 0 && __any_sync(0xffffffffu, need)) rescale_rows<D>(tO, alpha);
+          if (t > U.tlo[w] && __any_sync(0xffffffffu, need)) rescale_rows<D>(tO, alpha);
           const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
           l_run += exp_pack_store<BF16>(sr, m_use, tS);
         } else {
@@ -600,24 +653,28 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(bar(C::BAR_PFULL + w));
       }
+      if (!ok) break;
 
       // ---------------- epilogue: O * inv -> global ----------------
-      if (ok && bounded_wait(wc, bar(C::BAR_OFULL + w), 0)) {
-        ptx::tc_fence_after();
-        float inv;
-        if (SOFTMAX)
-          inv = (l_run > 0.f) ? 1.0f / l_run : 0.f;
-        else if (KIND == KIND_RELU)
-          inv = args.out_scale;
-        else
-          inv = 1.0f;
-        const bool row_ok = i < g.sq;
-        const int64_t real_row = static_cast<int64_t>(i) * args.vdil + r_res;
-        uint8_t *orow = reinterpret_cast<uint8_t *>(args.o) +
-                        2 * (b * args.o_sb + static_cast<int64_t>(h) * args.o_sh +
-                             real_row * args.o_ss);
-        store_rows<D, BF16>(tO, inv, row_ok, orow);
-      }
+      if (!bounded_wait(wc, bar(C::BAR_OFULL + w), units_w & 1)) break;
+      ptx::tc_fence_after();
+      float inv;
+      if (SOFTMAX)
+        inv = (l_run > 0.f) ? 1.0f / l_run : 0.f;
+      else if (KIND == KIND_RELU)
+        inv = args.out_scale;
+      else
+        inv = 1.0f;
+      const bool row_ok = i < g.sq;
+      const int64_t real_row = static_cast<int64_t>(i) * args.vdil + U.r_res;
+      uint8_t *orow = reinterpret_cast<uint8_t *>(args.o) +
+                      2 * (U.b * args.o_sb + static_cast<int64_t>(U.h) * args.o_sh +
+                           real_row * args.o_ss);
+      store_rows<D, BF16>(tO, inv, row_ok, orow);
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar(C::BAR_OEMPTY + w));
+      ++units_w;
     }
   }
 
@@ -627,6 +684,15 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
   if (warp == C::MMA_WARP) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+  if (threadIdx.x == 0 && args.sched != nullptr) {
+    // The last CTA to finish returns the scheduler to zero for the next launch;
+    // every CTA has made its final fetch before it counts itself finished.
+    __threadfence();
+    if (atomicAdd(args.sched + 1, 1) == static_cast<int>(gridDim.x) - 1) {
+      atomicExch(args.sched, 0);
+      atomicExch(args.sched + 1, 0);
+    }
   }
 }
 

@@ -70,6 +70,7 @@ _MODS = {"none": N.MOD_NONE, "softcap": N.MOD_SOFTCAP, "alibi": N.MOD_ALIBI,
          "temp": N.MOD_TEMP}
 
 _status_words: Dict[int, torch.Tensor] = {}
+_workspaces: Dict[int, torch.Tensor] = {}
 _param_cache: Dict[tuple, torch.Tensor] = {}
 
 
@@ -79,6 +80,17 @@ def _status_word(device: torch.device) -> torch.Tensor:
     if t is None:
         t = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
         _status_words[idx] = t
+    return t
+
+
+def _workspace(device: torch.device) -> torch.Tensor:
+    """Per-device scheduler workspace (zero-filled once; kernels leave it zeroed)."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    t = _workspaces.get(idx)
+    if t is None:
+        t = torch.zeros(N.WORKSPACE_BYTES // 4, dtype=torch.int32,
+                        device=torch.device("cuda", idx))
+        _workspaces[idx] = t
     return t
 
 
@@ -144,13 +156,17 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
               scale: Optional[float] = None, softcap: float = 30.0,
               head_param: Optional[Union[torch.Tensor, Sequence[float]]] = None,
               sig_bias: float = 0.0, out_scale: float = 1.0,
-              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+              out: Optional[torch.Tensor] = None, schedule: str = "dynamic") -> torch.Tensor:
     """Generic forward attention: ``norm(mask(mod(q.k * scale))) @ v``.
 
     ``q, k, v``: CUDA tensors ``[B, H, S, D]`` (bf16 / fp16; fp32 computed as
     bf16), ``D`` in {64, 128}. ``head_param``: ALiBi slopes (``mod="alibi"``)
-    or logit multipliers (``mod="temp"``), one per head.
+    or logit multipliers (``mod="temp"``), one per head. ``schedule``:
+    ``"dynamic"`` balances work units over the SMs with a per-device
+    workspace; ``"static"`` assigns them round-robin and uses no workspace.
     """
+    if schedule not in ("dynamic", "static"):
+        raise ValueError(f"unknown schedule {schedule!r}")
     if norm not in _NORMS or mod not in _MODS:
         raise ValueError(f"unknown norm/mod {norm!r}/{mod!r}")
     for name, t in (("q", q), ("k", k), ("v", v)):
@@ -208,6 +224,9 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     p.win_left, p.win_right = mask.left, mask.right
     p.block, p.prefix, p.dilation = mask.block, mask.prefix, mask.dilation
     p.status = _status_word(dev).data_ptr()
+    # One workspace per device: calls on different streams of one device would
+    # race on it, so only the current stream of the device is used here.
+    p.workspace = _workspace(dev).data_ptr() if schedule == "dynamic" else None
 
     lib = N.load()
     with torch.cuda.device(dev):

@@ -56,7 +56,10 @@ extern "C" {
 #define CHIA_API
 #endif
 
-#define CHIA_ATTN_ABI_VERSION 1
+#define CHIA_ATTN_ABI_VERSION 2
+
+/* Size of the optional scheduler workspace (bytes). */
+#define CHIA_ATTN_WORKSPACE_BYTES 256
 
 /* element types of q, k, v, o (all four share one type) */
 enum chia_dtype { CHIA_DTYPE_BF16 = 0, CHIA_DTYPE_F16 = 1 };
@@ -127,6 +130,13 @@ typedef struct chia_attn_params {
 
   int32_t *status; /* optional device int32; in-kernel errors are OR-ed in
                       (CHIA_ERR_DEVICE_TIMEOUT); caller zeroes it       */
+
+  /* optional device buffer of CHIA_ATTN_WORKSPACE_BYTES, zero-filled before
+   * its first use. It holds the counters of the load-balancing work
+   * scheduler; every call leaves it zeroed again. Calls that share one
+   * workspace must not run concurrently on the GPU. NULL selects a static
+   * round-robin schedule (no scratch memory at all). */
+  void *workspace;
 } chia_attn_params_t;
 
 /* Forward attention on `stream` (cudaStream_t; NULL = legacy default

@@ -235,3 +235,28 @@ def test_repeat_calls_are_deterministic(cuda):
     a = cp.bias_alibi(q, k, v, slopes=cp.alibi_slopes_geometric(4))
     for _ in range(3):
         assert torch.equal(a, cp.bias_alibi(q, k, v, slopes=cp.alibi_slopes_geometric(4)))
+
+
+@pytest.mark.parametrize("op", ["softcap_gemma2", "bias_sliding_window", "sigmoid_attn"])
+def test_static_and_dynamic_schedules_agree(cuda, op):
+    """Both work schedules run the same units; outputs are bit-identical, and
+    the dynamic scheduler leaves its workspace zeroed after every call."""
+    from chia_proj_b200 import ops
+    B, H, S, D = 3, 5, 1500, 128   # 6 query blocks x 15 heads = 90 units < 148 SMs
+    dev = torch.device("cuda", 0)
+    q, k, v = (t.to(dev) for t in gen(B, H, S, D, torch.bfloat16, seed=21))
+    mask = cp.op_config(op)
+    norm = "sigmoid" if op == "sigmoid_attn" else "softmax"
+    mod = "softcap" if op == "softcap_gemma2" else "none"
+    a = cp.attention(q, k, v, mask=mask, norm=norm, mod=mod, schedule="dynamic")
+    b = cp.attention(q, k, v, mask=mask, norm=norm, mod=mod, schedule="static")
+    assert torch.equal(a, b)
+    torch.cuda.synchronize()
+    assert int(ops._workspace(dev).abs().sum()) == 0
+    # many more units than SMs
+    q, k, v = (t.to(dev) for t in gen(8, 32, 1024, 64, torch.bfloat16, seed=22))
+    a = cp.attention(q, k, v, mask=mask, norm=norm, mod=mod, schedule="dynamic")
+    b = cp.attention(q, k, v, mask=mask, norm=norm, mod=mod, schedule="static")
+    assert torch.equal(a, b)
+    torch.cuda.synchronize()
+    assert int(ops._workspace(dev).abs().sum()) == 0
