@@ -479,6 +479,8 @@ def main(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--ref-step-seconds", type=float, default=3.0)
+    ap.add_argument("--suite-only", action="store_true",
+                    help="run only the per-variant suite at the north-star shape (1 GPU)")
     ap.add_argument("--units", type=int, default=B_TOTAL * H_TOTAL,
                     help="(batch, head) units in the job; smaller values are for ncu captures")
     a = ap.parse_args(argv)
@@ -486,6 +488,9 @@ def main(argv=None):
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if a.impl == "reference":
         run_reference(a)
+    elif a.suite_only:
+        torch.cuda.set_device(0)
+        print(json.dumps({"suite": headline_suite(torch.device("cuda", 0))}), flush=True)
     else:
         run_ours(a)
 

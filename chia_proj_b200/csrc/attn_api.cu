@@ -206,6 +206,17 @@ extern "C" {
 
 int chia_attn_abi_version(void) { return CHIA_ATTN_ABI_VERSION; }
 
+#ifdef CHIA_TRACE
+// Trace builds only (not part of the public ABI): copy the timeline buffer
+// of the last traced launch to host memory; returns bytes copied.
+__attribute__((visibility("default"))) long chia_attn_trace_read(void *dst, long bytes) {
+  const long n = bytes < static_cast<long>(sizeof(chia::g_chia_trace))
+                     ? bytes : static_cast<long>(sizeof(chia::g_chia_trace));
+  if (cudaMemcpyFromSymbol(dst, chia::g_chia_trace, n) != cudaSuccess) return -1;
+  return n;
+}
+#endif
+
 const char *chia_attn_status_string(int status) {
   switch (status) {
     case CHIA_OK: return "ok";

@@ -10,17 +10,17 @@
 //   warp 9     load warp: one thread issues every TMA load
 //
 // Tensor memory (512 columns x 128 lanes, fp32 cells):
-//   cols [  0,128)  S0 = Q0 K^T   (P0 is written back over its first BN/2 columns)
-//   cols [128,256)  S1 = Q1 K^T   (P1 likewise)
-//   cols [256,256+D) O0,  cols [384,384+D) O1   (fp32 output accumulators)
+//   cols [  0,128)  S0 = Q0 K^T,  cols [128,256)  S1 = Q1 K^T
+//   cols [256,256+D) O0,          cols [384,384+D) O1   (output accumulators)
+// Shared memory: Q0 Q1 | P0 P1 (16-bit softmax output) | K/V tile ring.
 //
-// Per key tile j the MMA warp issues S0(j), S1(j) (SS-UMMA, Q and K both
-// K-major in 128-byte-swizzled smem), and once softmax warpgroup w has written
-// P_w(j) into TMEM, O_w += P_w(j) V(j) (TS-UMMA: A = P from TMEM, B = V
-// MN-major in smem) followed immediately by S_w(j+1). UMMAs of one thread
-// execute in issue order, so the commit that signals "S_w(j+1) ready" also
-// proves that O_w has absorbed P_w(j): the softmax warpgroup may then rescale
-// O_w in TMEM without another barrier.
+// Pipeline per key tile j: as soon as softmax warpgroup w has copied S_w(j)
+// out of TMEM it releases the S_w columns, and the MMA warp computes
+// S_w(j+1) = Q_w K(j+1)^T into them while the warpgroup is still turning
+// S_w(j) into P_w(j); once P_w(j) is in shared memory the MMA warp issues
+// O_w += P_w(j) V(j). All UMMAs are SS (operands in 128-byte-swizzled smem:
+// Q, K and P K-major, V MN-major). The softmax warpgroup waits for
+// O_w += P_w(j-1) V(j-1) to retire before it overwrites P_w or rescales O_w.
 //
 // Normalisers: online softmax in the log2 domain with lazy rescaling (the
 // running max only moves when it grows by more than 8, i.e. a factor 256, so
@@ -80,22 +80,32 @@ struct FmhaConfig {
   static constexpr int KV_TILE_BYTES = BN * D * 2;
   static constexpr int CHUNK_Q_BYTES = BM * 128;
   static constexpr int CHUNK_KV_BYTES = BN * 128;
-  static constexpr int NS = (D == 128) ? 2 : 4;  // K ring and V ring depth
+  // P tiles (softmax output, 16-bit, 128 rows x BN keys) live in shared
+  // memory in the same 128-byte-swizzled K-major layout as Q, one per query
+  // tile, so the next S = Q K^T can be computed in TMEM while the softmax
+  // warpgroup still works on the current one.
+  static constexpr int P_TILE_BYTES = BM * BN * 2;
+  static constexpr int CHUNK_P_BYTES = BM * 128;
+  // One ring of NKV tile slots shared by K and V (slot = item % NKV). Items
+  // are loaded in the order the MMA warp consumes them: K of the first tile of
+  // a unit, then for each tile K of the next tile before V of this one.
+  static constexpr int NKV = (D == 128) ? 3 : 8;
   static constexpr int OFF_Q = 0;
-  static constexpr int OFF_K = OFF_Q + NQ * Q_TILE_BYTES;
-  static constexpr int OFF_V = OFF_K + NS * KV_TILE_BYTES;
-  static constexpr int OFF_BAR = OFF_V + NS * KV_TILE_BYTES;
-  // barriers: q q_empty | k_full[NS] k_empty[NS] v_full[NS] v_empty[NS] |
-  //           s_full[2] p_full[2] o_full[2] o_empty[2] | unit_full[2] unit_empty[2] | drain
+  static constexpr int OFF_P = OFF_Q + NQ * Q_TILE_BYTES;
+  static constexpr int OFF_KV = OFF_P + NQ * P_TILE_BYTES;
+  static constexpr int OFF_BAR = OFF_KV + NKV * KV_TILE_BYTES;
+  // barriers: q q_empty | kv_full[NKV] kv_empty[NKV] |
+  //           s_full[2] s_free[2] p_full[2] p_free[2] o_full[2] o_empty[2] |
+  //           unit_full[2] unit_empty[2] | drain
   static constexpr int BAR_Q = 0;
   static constexpr int BAR_QEMPTY = 1;
-  static constexpr int BAR_KFULL = 2;
-  static constexpr int BAR_KEMPTY = BAR_KFULL + NS;
-  static constexpr int BAR_VFULL = BAR_KEMPTY + NS;
-  static constexpr int BAR_VEMPTY = BAR_VFULL + NS;
-  static constexpr int BAR_SFULL = BAR_VEMPTY + NS;
-  static constexpr int BAR_PFULL = BAR_SFULL + NQ;
-  static constexpr int BAR_OFULL = BAR_PFULL + NQ;
+  static constexpr int BAR_KVFULL = 2;
+  static constexpr int BAR_KVEMPTY = BAR_KVFULL + NKV;
+  static constexpr int BAR_SFULL = BAR_KVEMPTY + NKV;
+  static constexpr int BAR_SFREE = BAR_SFULL + NQ;
+  static constexpr int BAR_PFULL = BAR_SFREE + NQ;
+  static constexpr int BAR_PFREE = BAR_PFULL + NQ;
+  static constexpr int BAR_OFULL = BAR_PFREE + NQ;
   static constexpr int BAR_OEMPTY = BAR_OFULL + NQ;
   static constexpr int BAR_UFULL = BAR_OEMPTY + NQ;
   static constexpr int BAR_UEMPTY = BAR_UFULL + 2;
@@ -112,11 +122,11 @@ struct FmhaConfig {
   static constexpr int THREADS = 384;
   static constexpr int MMA_WARP = 8;
   static constexpr int LOAD_WARP = 9;
-  static constexpr int REG_SOFTMAX = 216;
-  static constexpr int REG_OTHER = 72;
+  static constexpr int REG_SOFTMAX = 208;
+  static constexpr int REG_OTHER = 88;
   static_assert(2 * 128 * REG_SOFTMAX + 128 * REG_OTHER == THREADS * 168, "register split");
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t TMEM_S = 0;    // + w * 128
+  static constexpr uint32_t TMEM_S = 0;    // + w * 128 (fp32 S tile)
   static constexpr uint32_t TMEM_O = 256;  // + w * 128
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
@@ -127,6 +137,33 @@ struct WaitCtx {
   int32_t *status;
   uint64_t timeout_ns;
 };
+
+// ------------------------------------------------------------------------
+// Optional timeline tracing (compile with -DCHIA_TRACE; nothing is emitted
+// otherwise). CTA 0 records (tag, clock64) pairs per role into a static
+// device buffer that chia_attn_trace_read() copies out. Roles: 0/1 softmax
+// warpgroups (warp 0 / warp 4, lane 0), 2 MMA thread, 3 load thread.
+// ------------------------------------------------------------------------
+#ifdef CHIA_TRACE
+constexpr int kTraceEvents = 4096;
+__device__ unsigned long long g_chia_trace[4][kTraceEvents][2];
+struct Tracer {
+  int role, n;
+  __device__ __forceinline__ Tracer(int r) : role(r), n(0) {}
+  __device__ __forceinline__ void operator()(int tag) {
+    if (blockIdx.x == 0 && n < kTraceEvents) {
+      g_chia_trace[role][n][0] = static_cast<unsigned long long>(tag);
+      g_chia_trace[role][n][1] = clock64();
+      ++n;
+    }
+  }
+};
+#else
+struct Tracer {
+  __device__ __forceinline__ Tracer(int) {}
+  __device__ __forceinline__ void operator()(int) {}
+};
+#endif
 
 // Bounded wait on an mbarrier phase. Returns false (and raises the CTA abort
 // flag and the device status) when the wait expires or another warp aborted.
@@ -166,44 +203,67 @@ struct RowMask {
   int dil;
 };
 
-// Score -> modified, masked value, in place. MODE 0: tile fully visible (no
-// mask code at all); 1: band + prefix test; 2: band + prefix + dilation.
-// mx[c] receives the maximum of chunk c (softmax kinds only).
+// Visibility of column col for this thread's row (MODE 1: band + prefix,
+// MODE 2: also the dilation test).
+template <int MODE>
+__device__ __forceinline__ bool col_visible(const RowMask &rm, int col) {
+  bool vis = static_cast<uint32_t>(col - rm.c_lo) <= rm.span;
+  if (MODE == 2) vis = vis && ((rm.i_rel - col) % rm.dil) == 0;
+  return vis || (col < rm.c_pre);
+}
+
+// Softmax kinds, pass 1: score -> log2-domain logit x (modified and masked)
+// in place; returns the row maximum. Work is done on packed pairs of columns.
+// MODE 0: tile fully visible (no mask code); 1: band + prefix; 2: + dilation.
 template <int KIND, int MODE>
-__device__ __forceinline__ void transform_tile(uint32_t (&sr)[4][32], const EpiConsts &k,
-                                               const RowMask &rm, float (&mx)[4]) {
-  constexpr bool SOFTMAX = (KIND == KIND_SOFTMAX || KIND == KIND_SOFTCAP || KIND == KIND_ALIBI);
-  constexpr float MASKED = SOFTMAX ? -INFINITY : 0.0f;
+__device__ __forceinline__ float softmax_pass1(uint32_t (&sr)[4][32], const EpiConsts &k,
+                                               const RowMask &rm) {
+  const uint64_t K2 = ptx::f2(k.k_mul, k.k_mul);
+  const uint64_t CAP2 = ptx::f2(k.k_cap, k.k_cap);
+  const uint64_t KB2 = ptx::f2(k.k_bias, k.k_bias);
+  const uint64_t REL2 = ptx::f2(k.rel0, k.rel0 + 1.0f);
+  float m[4];
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    float m = -INFINITY;
+    float mc = -INFINITY;
 #pragma unroll
-    for (int e = 0; e < 32; ++e) {
+    for (int e = 0; e < 32; e += 2) {
       const int col = c * 32 + e;
-      const float s = __uint_as_float(sr[c][e]);
-      float x;
-      if (KIND == KIND_SOFTMAX) {
-        x = s * k.k_mul;
-      } else if (KIND == KIND_SOFTCAP) {
-        x = ptx::tanh_fast(s * k.k_mul) * k.k_cap;
+      uint64_t x2 = ptx::mul2(ptx::f2(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])), K2);
+      if (KIND == KIND_SOFTCAP) {
+        float a, b;
+        ptx::f2_split(x2, a, b);
+        x2 = ptx::mul2(ptx::f2(ptx::tanh_fast(a), ptx::tanh_fast(b)), CAP2);
       } else if (KIND == KIND_ALIBI) {
-        x = fmaf(k.k_bias, k.rel0 + static_cast<float>(col), s * k.k_mul);
-      } else if (KIND == KIND_SIGMOID) {
-        x = ptx::rcp_fast(1.0f + ptx::ex2(fmaf(s, k.k_mul, k.k_bias)));
-      } else {
-        x = fmaxf(s * k.k_mul, 0.0f);
+        // bias = slope * (j - i): (j - i) is formed exactly before scaling
+        const uint64_t rel = ptx::add2(REL2, ptx::f2(static_cast<float>(col), static_cast<float>(col)));
+        x2 = ptx::fma2(KB2, rel, x2);
       }
+      float a, b;
+      ptx::f2_split(x2, a, b);
       if (MODE != 0) {
-        bool vis = static_cast<uint32_t>(col - rm.c_lo) <= rm.span;
-        if (MODE == 2) vis = vis && ((rm.i_rel - col) % rm.dil) == 0;
-        vis = vis || (col < rm.c_pre);
-        x = vis ? x : MASKED;
+        if (!col_visible<MODE>(rm, col)) a = -INFINITY;
+        if (!col_visible<MODE>(rm, col + 1)) b = -INFINITY;
       }
-      if (SOFTMAX) m = fmaxf(m, x);
-      sr[c][e] = __float_as_uint(x);
+      mc = ptx::max3(mc, a, b);
+      sr[c][e] = __float_as_uint(a);
+      sr[c][e + 1] = __float_as_uint(b);
     }
-    mx[c] = m;
+    m[c] = mc;
   }
+  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+}
+
+// Write 64 keys (32 packed pairs) of this thread's P row into the
+// 128-byte-swizzled K-major P tile: 16-byte unit u of row r goes to unit
+// u ^ (r % 8), so the eight rows of a quarter-warp hit eight distinct bank
+// groups. prow = address of row r in chunk 0; chunk h2 holds keys 64*h2..+63.
+__device__ __forceinline__ void store_p_chunk(uint32_t prow, int h2, int rsw,
+                                              const uint32_t (&pk)[32]) {
+#pragma unroll
+  for (int u = 0; u < 8; ++u)
+    ptx::st_shared_v4(prow + h2 * (128 * 128) + ((u ^ rsw) << 4), pk[4 * u], pk[4 * u + 1],
+                      pk[4 * u + 2], pk[4 * u + 3]);
 }
 
 template <bool BF16>
@@ -211,44 +271,90 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return BF16 ? ptx::pack_bf16(lo, hi) : ptx::pack_f16(lo, hi);
 }
 
-// p = 2^(x - m), packed to 16-bit pairs and stored over the first 64 TMEM
-// columns of the S tile (32 columns at a time); returns the row sum of p.
+// Softmax pass 2: p = 2^(x - m), packed to 16-bit pairs and written to this
+// row of the shared-memory P tile; returns the row sum of p.
 template <bool BF16>
-__device__ __forceinline__ float exp_pack_store(uint32_t (&sr)[4][32], float m, uint32_t tS) {
-  float ls[4];
+__device__ __forceinline__ float softmax_pass2(uint32_t (&sr)[4][32], float m, uint32_t prow,
+                                               int rsw) {
+  const uint64_t NM2 = ptx::f2(-m, -m);
+  uint64_t acc[2] = {ptx::f2(0.f, 0.f), ptx::f2(0.f, 0.f)};
 #pragma unroll
   for (int h2 = 0; h2 < 2; ++h2) {
     uint32_t pk[32];
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
       const int c = 2 * h2 + cc;
-      float acc = 0.f;
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
-        const float p0 = ptx::ex2(__uint_as_float(sr[c][2 * e]) - m);
-        const float p1 = ptx::ex2(__uint_as_float(sr[c][2 * e + 1]) - m);
-        acc += p0 + p1;
-        pk[cc * 16 + e] = pack2<BF16>(p0, p1);
+      for (int e = 0; e < 32; e += 2) {
+        float a, b;
+        ptx::f2_split(ptx::add2(ptx::f2(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])), NM2),
+                      a, b);
+        const float p0 = ptx::ex2(a), p1 = ptx::ex2(b);
+        acc[cc] = ptx::add2(acc[cc], ptx::f2(p0, p1));
+        pk[cc * 16 + e / 2] = pack2<BF16>(p0, p1);
       }
-      ls[c] = acc;
     }
-    ptx::tmem_st32(tS + h2 * 32, pk);
+    store_p_chunk(prow, h2, rsw, pk);
   }
-  return (ls[0] + ls[1]) + (ls[2] + ls[3]);
+  float s0, s1, s2, s3;
+  ptx::f2_split(acc[0], s0, s1);
+  ptx::f2_split(acc[1], s2, s3);
+  return (s0 + s1) + (s2 + s3);
 }
 
-template <bool BF16>
-__device__ __forceinline__ void pack_store(uint32_t (&sr)[4][32], uint32_t tS) {
+// Non-softmax kinds: P = relu(s * scale) or sigmoid(s * scale + bias),
+// masked, packed and written to this row of the shared-memory P tile.
+// Sigmoid is 1 / (1 + 2^t): 2^t on the MUFU, the reciprocal on the FMA pipe
+// (initial guess from the exponent-field complement 0x7EF311C7 - bits(y),
+// then two Newton steps r <- r (2 - y r); relative error about 2e-4, below
+// the 2^-9 rounding of the 16-bit P).
+template <int KIND, int MODE, bool BF16>
+__device__ __forceinline__ void pointwise_tile(uint32_t (&sr)[4][32], const EpiConsts &k,
+                                               const RowMask &rm, uint32_t prow, int rsw) {
+  const uint64_t K2 = ptx::f2(k.k_mul, k.k_mul);
+  const uint64_t KB2 = ptx::f2(k.k_bias, k.k_bias);
+  const uint64_t NEG1 = ptx::f2(-1.0f, -1.0f);
+  const uint64_t TWO2 = ptx::f2(2.0f, 2.0f);
 #pragma unroll
   for (int h2 = 0; h2 < 2; ++h2) {
     uint32_t pk[32];
 #pragma unroll
-    for (int cc = 0; cc < 2; ++cc)
+    for (int cc = 0; cc < 2; ++cc) {
+      const int c = 2 * h2 + cc;
 #pragma unroll
-      for (int e = 0; e < 16; ++e)
-        pk[cc * 16 + e] = pack2<BF16>(__uint_as_float(sr[2 * h2 + cc][2 * e]),
-                                      __uint_as_float(sr[2 * h2 + cc][2 * e + 1]));
-    ptx::tmem_st32(tS + h2 * 32, pk);
+      for (int e = 0; e < 32; e += 2) {
+        const int col = c * 32 + e;
+        const uint64_t s2 = ptx::f2(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
+        float a, b;
+        if (KIND == KIND_RELU) {
+          ptx::f2_split(ptx::mul2(s2, K2), a, b);
+          if (MODE != 0) {
+            if (!col_visible<MODE>(rm, col)) a = 0.f;
+            if (!col_visible<MODE>(rm, col + 1)) b = 0.f;
+          }
+          pk[cc * 16 + e / 2] = BF16 ? ptx::pack_bf16_relu(a, b) : ptx::pack_f16_relu(a, b);
+        } else {
+          // t = -(s*scale + bias) * log2(e), clamped so 2^t stays finite
+          float t0, t1;
+          ptx::f2_split(ptx::fma2(s2, K2, KB2), t0, t1);
+          const uint64_t e2 = ptx::f2(ptx::ex2(fminf(t0, 126.f)), ptx::ex2(fminf(t1, 126.f)));
+          const uint64_t ny = ptx::fma2(e2, NEG1, NEG1);  // -(1 + 2^t)
+          float y0, y1;
+          ptx::f2_split(ny, y0, y1);
+          uint64_t r = ptx::f2(__uint_as_float(0xFEF311C7u - __float_as_uint(y0)),
+                               __uint_as_float(0xFEF311C7u - __float_as_uint(y1)));
+          r = ptx::mul2(r, ptx::fma2(ny, r, TWO2));
+          r = ptx::mul2(r, ptx::fma2(ny, r, TWO2));
+          ptx::f2_split(r, a, b);
+          if (MODE != 0) {
+            if (!col_visible<MODE>(rm, col)) a = 0.f;
+            if (!col_visible<MODE>(rm, col + 1)) b = 0.f;
+          }
+          pk[cc * 16 + e / 2] = pack2<BF16>(a, b);
+        }
+      }
+    }
+    store_p_chunk(prow, h2, rsw, pk);
   }
 }
 
@@ -336,7 +442,7 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
                     const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const KernelArgs args) {
   using C = FmhaConfig<D>;
-  constexpr int BM = C::BM, BN = C::BN, NQ = C::NQ, NS = C::NS;
+  constexpr int BM = C::BM, BN = C::BN, NQ = C::NQ, NKV = C::NKV;
   constexpr bool SOFTMAX = (KIND == KIND_SOFTMAX || KIND == KIND_SOFTCAP || KIND == KIND_ALIBI);
   constexpr float LOG2E = 1.4426950408889634f;
 
@@ -357,15 +463,15 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
   if (threadIdx.x == 0) {
     ptx::mbar_init(bar(C::BAR_Q), 1);
     ptx::mbar_init(bar(C::BAR_QEMPTY), 1);
-    for (int s = 0; s < NS; ++s) {
-      ptx::mbar_init(bar(C::BAR_KFULL + s), 1);
-      ptx::mbar_init(bar(C::BAR_KEMPTY + s), 1);
-      ptx::mbar_init(bar(C::BAR_VFULL + s), 1);
-      ptx::mbar_init(bar(C::BAR_VEMPTY + s), 1);
+    for (int s = 0; s < NKV; ++s) {
+      ptx::mbar_init(bar(C::BAR_KVFULL + s), 1);
+      ptx::mbar_init(bar(C::BAR_KVEMPTY + s), 1);
     }
     for (int w = 0; w < NQ; ++w) {
       ptx::mbar_init(bar(C::BAR_SFULL + w), 1);
+      ptx::mbar_init(bar(C::BAR_SFREE + w), 4);   // one arrive per softmax warp
       ptx::mbar_init(bar(C::BAR_PFULL + w), 4);   // one arrive per softmax warp
+      ptx::mbar_init(bar(C::BAR_PFREE + w), 1);
       ptx::mbar_init(bar(C::BAR_OFULL + w), 1);
       ptx::mbar_init(bar(C::BAR_OEMPTY + w), 4);  // one arrive per softmax warp
     }
@@ -397,9 +503,24 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
     ptx::setmaxnreg_dec<C::REG_OTHER>();
     if (warp == C::LOAD_WARP && lane == 0) {
       // ==================== scheduler + TMA producer ====================
-      uint32_t it = 0;
-      int64_t last_use[2 * NS];
-      for (int s = 0; s < 2 * NS; ++s) last_use[s] = -1;
+      Tracer tr(3);
+      uint32_t n = 0;  // ring items issued (K and V of every tile)
+      int64_t last_item[NKV];
+      for (int s = 0; s < NKV; ++s) last_item[s] = -1;
+      auto load_item = [&](const CUtensorMap *map, int64_t j, const UnitInfo &U) -> bool {
+        const int s = n % NKV;
+        if (!bounded_wait(wc, bar(C::BAR_KVEMPTY + s), ((n / NKV) & 1) ^ 1)) return false;
+        tr(30);  // ring slot free, issuing a K or V tile
+        ptx::mbar_arrive_expect_tx(bar(C::BAR_KVFULL + s), C::KV_TILE_BYTES);
+#pragma unroll
+        for (int c = 0; c < C::NCHUNK; ++c)
+          ptx::tma_load_5d(sbase + C::OFF_KV + s * C::KV_TILE_BYTES + c * C::CHUNK_KV_BYTES, map,
+                           bar(C::BAR_KVFULL + s), c * 64, static_cast<int>(j * BN), U.r_res,
+                           U.h, U.b);
+        last_item[s] = n;
+        ++n;
+        return true;
+      };
       for (int k = 0;; ++k) {
         const int slot = k & 1;
         if (!bounded_wait(wc, bar(C::BAR_UEMPTY + slot), ((k >> 1) & 1) ^ 1)) break;
@@ -425,68 +546,70 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
               ptx::tma_load_5d(sbase + C::OFF_Q + w * C::Q_TILE_BYTES + c * C::CHUNK_Q_BYTES,
                                &tm_q, bar(C::BAR_Q), c * 64, static_cast<int>(U.m0 + w * BM),
                                U.r_res, U.h, U.b);
-        bool ok = true;
-        for (int64_t j = U.jlo; j < U.jhi; ++j) {
-          if (!U.any_active(j)) continue;
-          const int s = it % NS;
-          const uint32_t ph = (it / NS) & 1;
-          if (!bounded_wait(wc, bar(C::BAR_KEMPTY + s), ph ^ 1)) { ok = false; break; }
-          ptx::mbar_arrive_expect_tx(bar(C::BAR_KFULL + s), C::KV_TILE_BYTES);
-#pragma unroll
-          for (int c = 0; c < C::NCHUNK; ++c)
-            ptx::tma_load_5d(sbase + C::OFF_K + s * C::KV_TILE_BYTES + c * C::CHUNK_KV_BYTES,
-                             &tm_k, bar(C::BAR_KFULL + s), c * 64, static_cast<int>(j * BN),
-                             U.r_res, U.h, U.b);
-          last_use[s] = it;
-          if (!bounded_wait(wc, bar(C::BAR_VEMPTY + s), ph ^ 1)) { ok = false; break; }
-          ptx::mbar_arrive_expect_tx(bar(C::BAR_VFULL + s), C::KV_TILE_BYTES);
-#pragma unroll
-          for (int c = 0; c < C::NCHUNK; ++c)
-            ptx::tma_load_5d(sbase + C::OFF_V + s * C::KV_TILE_BYTES + c * C::CHUNK_KV_BYTES,
-                             &tm_v, bar(C::BAR_VFULL + s), c * 64, static_cast<int>(j * BN),
-                             U.r_res, U.h, U.b);
-          last_use[NS + s] = it;
-          ++it;
+        // K(jlo), then K(j+1) before V(j): ring position of K_i is 2i-1
+        // (K_0 at 0), of V_i 2i+2, of the last V 2T-1 (T tiles in the unit)
+        bool ok = load_item(&tm_k, U.jlo, U);
+        for (int64_t j = U.jlo; ok && j < U.jhi; ++j) {
+          if (j + 1 < U.jhi) ok = load_item(&tm_k, j + 1, U);
+          ok = ok && load_item(&tm_v, j, U);
         }
         if (!ok) break;
       }
       // Drain: every copy this thread issued lands before the CTA exits (the
       // Q copies complete before the MMA thread can finish its last unit).
-      for (int s = 0; s < NS; ++s) {
-        if (last_use[s] >= 0)
-          bounded_wait(wc, bar(C::BAR_KFULL + s), (last_use[s] / NS) & 1, false);
-        if (last_use[NS + s] >= 0)
-          bounded_wait(wc, bar(C::BAR_VFULL + s), (last_use[NS + s] / NS) & 1, false);
-      }
+      for (int s = 0; s < NKV; ++s)
+        if (last_item[s] >= 0)
+          bounded_wait(wc, bar(C::BAR_KVFULL + s), (last_item[s] / NKV) & 1, false);
     } else if (warp == C::MMA_WARP && lane == 0) {
       // =========================== UMMA issuer ===========================
       constexpr uint32_t IDESC_QK = ptx::make_idesc_f16(BM, BN, BF16, false, false);
       constexpr uint32_t IDESC_PV = ptx::make_idesc_f16(BM, D, BF16, false, true);
-      const uint32_t q_s = sbase + C::OFF_Q, k_s = sbase + C::OFF_K, v_s = sbase + C::OFF_V;
+      const uint32_t q_s = sbase + C::OFF_Q, p_s = sbase + C::OFF_P, kv_s = sbase + C::OFF_KV;
 
+      // Descriptor of each operand at k-step 0; the start-address field (bits
+      // 0-13, address >> 4) is then advanced by plain adds: shared memory
+      // addresses stay below 256 KB, so the field never carries.
+      const uint64_t dq = ptx::make_sdesc_sw128(q_s, 16, 1024);
+      const uint64_t dp = ptx::make_sdesc_sw128(p_s, 16, 1024);
+      const uint64_t dk = ptx::make_sdesc_sw128(kv_s, 16, 1024);
+      const uint64_t dv = ptx::make_sdesc_sw128(kv_s, C::CHUNK_KV_BYTES, 1024);
       auto issue_s = [&](int w, int stage) {
         const uint32_t d_tmem = tmem_base + C::TMEM_S + w * 128;
+        const uint64_t a0 = dq + ((w * C::Q_TILE_BYTES) >> 4);
+        const uint64_t b0 = dk + ((stage * C::KV_TILE_BYTES) >> 4);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk & 3) * 32;
-          const uint32_t qa = q_s + w * C::Q_TILE_BYTES + (kk >> 2) * C::CHUNK_Q_BYTES + off;
-          const uint32_t ka = k_s + stage * C::KV_TILE_BYTES + (kk >> 2) * C::CHUNK_KV_BYTES + off;
-          ptx::umma_ss(d_tmem, ptx::make_sdesc_sw128(qa, 16, 1024),
-                       ptx::make_sdesc_sw128(ka, 16, 1024), IDESC_QK, kk > 0 ? 1u : 0u);
+          const uint32_t off = ((kk >> 2) * C::CHUNK_Q_BYTES + (kk & 3) * 32) >> 4;
+          const uint32_t offk = ((kk >> 2) * C::CHUNK_KV_BYTES + (kk & 3) * 32) >> 4;
+          ptx::umma_ss(d_tmem, a0 + off, b0 + offk, IDESC_QK, kk > 0 ? 1u : 0u);
         }
       };
       auto issue_pv = [&](int w, int stage, bool first) {
         const uint32_t d_tmem = tmem_base + C::TMEM_O + w * 128;
-        const uint32_t p_tmem = tmem_base + C::TMEM_S + w * 128;
+        const uint64_t a0 = dp + ((w * C::P_TILE_BYTES) >> 4);
+        const uint64_t b0 = dv + ((stage * C::KV_TILE_BYTES) >> 4);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint32_t va = v_s + stage * C::KV_TILE_BYTES + kk * 2048;
-          ptx::umma_ts(d_tmem, p_tmem + kk * 8, ptx::make_sdesc_sw128(va, C::CHUNK_KV_BYTES, 1024),
-                       IDESC_PV, (first && kk == 0) ? 0u : 1u);
+          const uint32_t offp = ((kk >> 2) * C::CHUNK_P_BYTES + (kk & 3) * 32) >> 4;
+          ptx::umma_ss(d_tmem, a0 + offp, b0 + ((kk * 2048) >> 4), IDESC_PV,
+                       (first && kk == 0) ? 0u : 1u);
         }
       };
 
-      uint32_t kit = 0, vit = 0, pcnt[NQ] = {0, 0}, units_w[NQ] = {0, 0};
+      Tracer tr(2);
+      // Event-driven issue: the thread polls every pending step of both query
+      // tiles and issues whichever is ready, so neither softmax warpgroup
+      // waits behind the other.
+      //   S_w(t)  needs K(t) resident and S_w(t-1) copied out of TMEM (s_free)
+      //   PV_w(t) needs P_w(t) written (p_full), V(t) resident, and for the
+      //           first tile of a unit the previous epilogue done (o_empty)
+      // A K / V ring slot is released once every query tile that uses it has
+      // issued its MMA (and the copy into it has landed).
+      uint32_t base = 0;  // ring position of the current unit's first item
+      uint32_t scnt[NQ] = {0, 0}, pcnt[NQ] = {0, 0}, units_w[NQ] = {0, 0};
+      auto test_item = [&](uint32_t item) {
+        return ptx::mbar_test_wait(bar(C::BAR_KVFULL + item % NKV), (item / NKV) & 1);
+      };
       bool ok = true;
       for (int k = 0; ok; ++k) {
         const int slot = k & 1;
@@ -497,57 +620,98 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
         UnitInfo U;
         decode_unit<BM, BN>(u, args, U);
         if (!bounded_wait(wc, bar(C::BAR_Q), k & 1)) break;
-        if (!bounded_wait(wc, bar(C::BAR_KFULL + kit % NS), (kit / NS) & 1)) break;
-        ptx::tc_fence_after();
+        const int jlo = static_cast<int>(U.jlo), T = static_cast<int>(U.jhi - U.jlo);
+        auto kpos = [&](int i) { return base + static_cast<uint32_t>(i == 0 ? 0 : 2 * i - 1); };
+        auto vpos = [&](int i) {
+          return base + static_cast<uint32_t>(i < T - 1 ? 2 * i + 2 : 2 * T - 1);
+        };
+        int sn[NQ], pn[NQ], lo[NQ], hi[NQ];
 #pragma unroll
-        for (int w = 0; w < NQ; ++w)
-          if (U.active(w, U.jlo)) {
-            issue_s(w, kit % NS);
-            ptx::umma_commit(bar(C::BAR_SFULL + w));
-          }
-        ptx::umma_commit(bar(C::BAR_KEMPTY + kit % NS));
-        ++kit;
-        bool first[NQ] = {true, true};
-        for (int64_t j = U.jlo; j < U.jhi;) {
-          int64_t jn = j + 1;
-          while (jn < U.jhi && !U.any_active(jn)) ++jn;
-          const bool has_next = jn < U.jhi;
-          if (!has_next) ptx::umma_commit(bar(C::BAR_QEMPTY));  // every S of this unit issued
-          const int vs = vit % NS;
-          const int ks = kit % NS;
-          if (!bounded_wait(wc, bar(C::BAR_VFULL + vs), (vit / NS) & 1)) { ok = false; break; }
-          if (has_next && !bounded_wait(wc, bar(C::BAR_KFULL + ks), (kit / NS) & 1)) { ok = false; break; }
-          ptx::tc_fence_after();
+        for (int w = 0; w < NQ; ++w) {
+          lo[w] = static_cast<int>(U.tlo[w]);
+          hi[w] = static_cast<int>(U.thi[w]);
+          sn[w] = pn[w] = lo[w];
+        }
+        auto user = [&](int w, int t) { return t >= lo[w] && t < hi[w]; };
+        int krel = 0, vrel = 0;  // next K / V item (tile offset) to release
+        bool q_released = false;
+        uint64_t idle_since = 0;
+        while (true) {
+          bool progress = false;
 #pragma unroll
           for (int w = 0; w < NQ; ++w) {
-            if (U.active(w, j)) {
-              if (!bounded_wait(wc, bar(C::BAR_PFULL + w), pcnt[w] & 1)) { ok = false; break; }
-              ++pcnt[w];
-              // the previous unit's epilogue must have read O_w before it is overwritten
-              if (first[w] && units_w[w] > 0 &&
-                  !bounded_wait(wc, bar(C::BAR_OEMPTY + w), (units_w[w] - 1) & 1)) { ok = false; break; }
-              ptx::tc_fence_after();
-              issue_pv(w, vs, first[w]);
-              first[w] = false;
-              if (j == U.thi[w] - 1) {
-                ptx::umma_commit(bar(C::BAR_OFULL + w));
-                ++units_w[w];
+            if (sn[w] < hi[w]) {
+              const uint32_t it = kpos(sn[w] - jlo);
+              if (test_item(it) &&
+                  (scnt[w] == 0 || ptx::mbar_test_wait(bar(C::BAR_SFREE + w), (scnt[w] - 1) & 1))) {
+                ptx::tc_fence_after();
+                issue_s(w, it % NKV);
+                ptx::umma_commit(bar(C::BAR_SFULL + w));
+                ++scnt[w];
+                ++sn[w];
+                progress = true;
+                tr(20 + w);  // S_w issued
               }
             }
-            if (has_next && U.active(w, jn)) {
-              issue_s(w, ks);
-              ptx::umma_commit(bar(C::BAR_SFULL + w));
+            if (pn[w] < hi[w]) {
+              const uint32_t it = vpos(pn[w] - jlo);
+              const bool first = pn[w] == lo[w];
+              if (ptx::mbar_test_wait(bar(C::BAR_PFULL + w), pcnt[w] & 1) && test_item(it) &&
+                  (!first || units_w[w] == 0 ||
+                   ptx::mbar_test_wait(bar(C::BAR_OEMPTY + w), (units_w[w] - 1) & 1))) {
+                ptx::tc_fence_after();
+                issue_pv(w, it % NKV, first);
+                ptx::umma_commit(bar(C::BAR_PFREE + w));
+                ++pcnt[w];
+                if (pn[w] == hi[w] - 1) {
+                  ptx::umma_commit(bar(C::BAR_OFULL + w));
+                  ++units_w[w];
+                }
+                ++pn[w];
+                progress = true;
+                tr(22 + w);  // PV_w issued
+              }
             }
           }
-          if (!ok) break;
-          ptx::umma_commit(bar(C::BAR_VEMPTY + vs));
-          ++vit;
-          if (has_next) {
-            ptx::umma_commit(bar(C::BAR_KEMPTY + ks));
-            ++kit;
+          // release ring items, in order, once all their users have issued
+          while (krel < T) {
+            const int t = jlo + krel;
+            if ((user(0, t) && sn[0] <= t) || (user(1, t) && sn[1] <= t)) break;
+            const uint32_t it = kpos(krel);
+            if (!test_item(it)) break;  // an unused item must still have landed
+            ptx::umma_commit(bar(C::BAR_KVEMPTY + it % NKV));
+            ++krel;
           }
-          j = jn;
+          while (vrel < T) {
+            const int t = jlo + vrel;
+            if ((user(0, t) && pn[0] <= t) || (user(1, t) && pn[1] <= t)) break;
+            const uint32_t it = vpos(vrel);
+            if (!test_item(it)) break;
+            ptx::umma_commit(bar(C::BAR_KVEMPTY + it % NKV));
+            ++vrel;
+          }
+          if (!q_released && sn[0] >= hi[0] && sn[1] >= hi[1]) {
+            ptx::umma_commit(bar(C::BAR_QEMPTY));  // every S of this unit issued
+            q_released = true;
+          }
+          if (krel >= T && vrel >= T && pn[0] >= hi[0] && pn[1] >= hi[1]) break;
+          if (progress) {
+            idle_since = 0;
+          } else {
+            // nothing ready: back off briefly, bounded like every other wait
+            const uint64_t now = ptx::globaltimer_ns();
+            if (idle_since == 0) idle_since = now;
+            if (*abort_flag) { ok = false; break; }
+            if (now - idle_since > args.timeout_ns) {
+              *abort_flag = 1;
+              if (args.status) atomicOr(args.status, 5 /* CHIA_ERR_DEVICE_TIMEOUT */);
+              ok = false;
+              break;
+            }
+            __nanosleep(20);
+          }
         }
+        base += 2 * static_cast<uint32_t>(T);
       }
       // Drain: all UMMAs issued by this thread complete before TMEM is freed.
       ptx::umma_commit(bar(C::BAR_DRAIN));
@@ -563,10 +727,15 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
     const uint32_t tS = tmem_base + lane_off + C::TMEM_S + w * 128;
     const uint32_t tO = tmem_base + lane_off + C::TMEM_O + w * 128;
+    const uint32_t prow = sbase + C::OFF_P + w * C::P_TILE_BYTES + row * 128;  // this row of P_w
+    const int rsw = row & 7;
     const int prefix = static_cast<int>(g.prefix);
     const int dil = static_cast<int>(g.dil);
     const float score_scale = args.score_scale;
 
+    Tracer tr(warp == 0 ? 0 : 1);
+    const bool tracing = (warp & 3) == 0 && lane == 0;
+    auto trs = [&](int tag) { if (tracing) tr(tag); };
     uint32_t cnt = 0, units_w = 0;
     for (int k = 0;; ++k) {
       const int slot = k & 1;
@@ -609,13 +778,19 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
       bool ok = true;
       for (int64_t t = U.tlo[w]; t < U.thi[w]; ++t, ++cnt) {
         if (!bounded_wait(wc, bar(C::BAR_SFULL + w), cnt & 1)) { ok = false; break; }
+        trs(10);  // S ready
         ptx::tc_fence_after();
         uint32_t sr[4][32];
 #pragma unroll
         for (int c = 0; c < 4; ++c) ptx::tmem_ld32(tS + c * 32, sr[c]);
         ptx::tmem_wait_ld();
+        trs(11);  // S in registers
 #pragma unroll
         for (int c = 0; c < 4; ++c) ptx::reg_fence(sr[c]);
+        // S_w is in registers: its TMEM columns may take the next tile
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(bar(C::BAR_SFREE + w));
 
         const int kv0 = static_cast<int>(t) * BN;
         RowMask rm;
@@ -625,16 +800,20 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
         rm.i_rel = i - kv0;
         rm.dil = dil;
         kc.rel0 = static_cast<float>(kv0 - i);  // (j - i) of column 0, exact in fp32
-        float mx[4];
-        if (tile_full(g, r0, r1, BN, t))
-          transform_tile<KIND, 0>(sr, kc, rm, mx);
-        else if (dil == 1)
-          transform_tile<KIND, 1>(sr, kc, rm, mx);
-        else
-          transform_tile<KIND, 2>(sr, kc, rm, mx);
-
+        const int mode = tile_full(g, r0, r1, BN, t) ? 0 : (dil == 1 ? 1 : 2);
         if (SOFTMAX) {
-          const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])));
+          float mx;
+          if (mode == 0)
+            mx = softmax_pass1<KIND, 0>(sr, kc, rm);
+          else if (mode == 1)
+            mx = softmax_pass1<KIND, 1>(sr, kc, rm);
+          else
+            mx = softmax_pass1<KIND, 2>(sr, kc, rm);
+          trs(12);  // mod + mask done
+          // P_w and O_w may only change once O_w += P_w V of the previous tile retired
+          if (cnt > 0 && !bounded_wait(wc, bar(C::BAR_PFREE + w), (cnt - 1) & 1)) { ok = false; break; }
+          ptx::tc_fence_after();
+          const float m_new = fmaxf(m_run, mx);
           const bool need = m_new > m_run + 8.0f;
           float alpha = 1.0f;
           if (need) {
@@ -644,14 +823,24 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
           }
           if (t > U.tlo[w] && __any_sync(0xffffffffu, need)) rescale_rows<D>(tO, alpha);
           const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-          l_run += exp_pack_store<BF16>(sr, m_use, tS);
+          l_run += softmax_pass2<BF16>(sr, m_use, prow, rsw);
         } else {
-          pack_store<BF16>(sr, tS);
+          if (cnt > 0 && !bounded_wait(wc, bar(C::BAR_PFREE + w), (cnt - 1) & 1)) { ok = false; break; }
+          if (mode == 0)
+            pointwise_tile<KIND, 0, BF16>(sr, kc, rm, prow, rsw);
+          else if (mode == 1)
+            pointwise_tile<KIND, 1, BF16>(sr, kc, rm, prow, rsw);
+          else
+            pointwise_tile<KIND, 2, BF16>(sr, kc, rm, prow, rsw);
+          trs(12);
         }
-        ptx::tmem_wait_st();
+        ptx::tmem_wait_st();  // O rescale stores (rare)
+        // generic-proxy P writes must be visible to the UMMA (async proxy)
+        ptx::fence_proxy_async_smem();
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(bar(C::BAR_PFULL + w));
+        trs(13);  // P stored and signalled
       }
       if (!ok) break;
 
@@ -670,7 +859,9 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
       uint8_t *orow = reinterpret_cast<uint8_t *>(args.o) +
                       2 * (U.b * args.o_sb + static_cast<int64_t>(U.h) * args.o_sh +
                            real_row * args.o_ss);
+      trs(14);  // O ready
       store_rows<D, BF16>(tO, inv, row_ok, orow);
+      trs(15);  // O stored
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar(C::BAR_OEMPTY + w));
