@@ -22,7 +22,7 @@
 #include <mutex>
 
 #include "../../include/chia_attn.h"
-#include "fmha_sm100.cuh"
+#include "fmha2_sm100.cuh"
 
 namespace {
 
@@ -87,6 +87,9 @@ int validate(const chia_attn_params_t *p) {
   if (p->norm != CHIA_NORM_SOFTMAX && p->mod != CHIA_MOD_NONE) return CHIA_ERR_UNSUPPORTED;
   if (p->batch < 1 || p->heads < 1 || p->seqlen_q < 1 || p->seqlen_kv < 1)
     return CHIA_ERR_INVALID_ARGUMENT;
+  // With S_q <= S_kv the diagonal key j = i is visible for every row under
+  // every mask this ABI can describe, so no query row is left without keys.
+  if (p->seqlen_q > p->seqlen_kv) return CHIA_ERR_UNSUPPORTED;
   if (p->seqlen_q > (int64_t(1) << 30) || p->seqlen_kv > (int64_t(1) << 30) ||
       p->heads > (int64_t(1) << 24) || p->batch > (int64_t(1) << 24))
     return CHIA_ERR_UNSUPPORTED;
@@ -124,10 +127,10 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 5-D view (D, S', vdil, H, B) of a [B, H, S, D] tensor; box (64, 128, 1, 1, 1),
-// 128-byte swizzle, zero fill out of bounds.
+// 5-D view (D, S', vdil, H, B) of a [B, H, S, D] tensor; box (64, box_rows,
+// 1, 1, 1), 128-byte swizzle, zero fill out of bounds.
 bool encode_map(CUtensorMap *map, const void *base, int dtype, int64_t D, int64_t s_virtual,
-                int vdil, int64_t H, int64_t B, const int64_t *stride_el) {
+                int vdil, int64_t H, int64_t B, const int64_t *stride_el, uint32_t box_rows = 128) {
   auto fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[5] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(s_virtual),
@@ -137,7 +140,7 @@ bool encode_map(CUtensorMap *map, const void *base, int dtype, int64_t D, int64_
                                  static_cast<cuuint64_t>(stride_el[2] * 2),
                                  static_cast<cuuint64_t>(stride_el[1] * 2),
                                  static_cast<cuuint64_t>(stride_el[0] * 2)};
-  const cuuint32_t box[5] = {64, 128, 1, 1, 1};
+  const cuuint32_t box[5] = {64, box_rows, 1, 1, 1};
   const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
   const CUtensorMapDataType dt =
       dtype == CHIA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
@@ -175,6 +178,51 @@ int launch_one(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &
   }
   kern<<<static_cast<unsigned>(nblocks), Cfg::THREADS, Cfg::SMEM_ALLOC, stream>>>(mq, mk, mv, a);
   return cudaGetLastError() == cudaSuccess ? CHIA_OK : CHIA_ERR_LAUNCH;
+}
+
+// head_dim 128: CTA pairs with 2-SM UMMAs (fmha2_sm100.cuh)
+template <bool BF16, int KIND>
+int launch_pair(const CUtensorMap &mq, const CUtensorMap &mkh, const CUtensorMap &mvh,
+                const chia::KernelArgs &a, int64_t nunits, cudaStream_t stream) {
+  using Cfg = chia::Fmha2Config<128>;
+  auto kern = chia::fmha2_fwd_kernel<128, BF16, KIND>;
+  static std::atomic<uint32_t> configured{0};
+  static std::atomic<int> max_pairs[32];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHIA_ERR_NO_DEVICE;
+  const uint32_t bit = 1u << (dev & 31);
+  if (!(configured.load(std::memory_order_acquire) & bit)) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_ALLOC) !=
+        cudaSuccess)
+      return CHIA_ERR_LAUNCH;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(Cfg::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::SMEM_ALLOC;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess || clusters < 1)
+      return CHIA_ERR_LAUNCH;
+    max_pairs[dev & 31].store(clusters, std::memory_order_relaxed);
+    configured.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  const int64_t pairs_max = max_pairs[dev & 31].load(std::memory_order_relaxed);
+  const int64_t pairs = nunits < pairs_max ? nunits : pairs_max;
+  kern<<<static_cast<unsigned>(2 * pairs), Cfg::THREADS, Cfg::SMEM_ALLOC, stream>>>(mq, mkh, mvh,
+                                                                                   a);
+  return cudaGetLastError() == cudaSuccess ? CHIA_OK : CHIA_ERR_LAUNCH;
+}
+
+template <bool BF16>
+int launch_pair_kind(int kind, const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
+                     const chia::KernelArgs &a, int64_t nunits, cudaStream_t s) {
+  switch (kind) {
+    case chia::KIND_SOFTMAX: return launch_pair<BF16, chia::KIND_SOFTMAX>(mq, mk, mv, a, nunits, s);
+    case chia::KIND_SOFTCAP: return launch_pair<BF16, chia::KIND_SOFTCAP>(mq, mk, mv, a, nunits, s);
+    case chia::KIND_ALIBI: return launch_pair<BF16, chia::KIND_ALIBI>(mq, mk, mv, a, nunits, s);
+    case chia::KIND_SIGMOID: return launch_pair<BF16, chia::KIND_SIGMOID>(mq, mk, mv, a, nunits, s);
+    case chia::KIND_RELU: return launch_pair<BF16, chia::KIND_RELU>(mq, mk, mv, a, nunits, s);
+  }
+  return CHIA_ERR_INVALID_ARGUMENT;
 }
 
 template <int D, bool BF16>
@@ -309,9 +357,15 @@ int chia_attn_fwd(const chia_attn_params_t *p, void *stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int kind = kind_of(p);
   const bool bf16 = p->dtype == CHIA_DTYPE_BF16;
-  if (D == 128)
-    return bf16 ? launch_kind<128, true>(kind, mq, mk, mv, a, nblocks, s)
-                : launch_kind<128, false>(kind, mq, mk, mv, a, nblocks, s);
+  if (D == 128) {
+    // K in half tiles of 64 keys (one per CTA of the pair); V as loaded above
+    // (box of 128 keys x 64 columns; each CTA takes one column chunk)
+    CUtensorMap mkh;
+    if (!encode_map(&mkh, p->k, p->dtype, D, g.skv, dv.vdil, p->heads, p->batch, p->k_stride, 64))
+      return CHIA_ERR_LAUNCH;
+    return bf16 ? launch_pair_kind<true>(kind, mq, mkh, mv, a, nunits, s)
+                : launch_pair_kind<false>(kind, mq, mkh, mv, a, nunits, s);
+  }
   return bf16 ? launch_kind<64, true>(kind, mq, mk, mv, a, nblocks, s)
               : launch_kind<64, false>(kind, mq, mk, mv, a, nblocks, s);
 }

@@ -1,0 +1,496 @@
+// fmha2_sm100.cuh -- head_dim 128 forward attention on CTA pairs (2-SM UMMA).
+//
+// A cluster of two CTAs on two SMs computes one work unit of 256 query rows:
+// CTA rank r owns query tile r (128 rows). Every UMMA is a cta_group::2 MMA
+// with M = 256 issued by the even CTA:
+//   S = Q K^T   A = Q (each CTA its own 128 rows, smem), B = K tile of 128
+//               keys split by keys: CTA r holds keys [64r, 64r+64)
+//   O += P V    A = P (each CTA's TMEM), B = V tile split by feature columns:
+//               CTA r holds columns [64r, 64r+64)
+// so each SM reads a full A and half a B per MMA: 96 bytes/clock of shared
+// memory at the tensor core's full rate (a single-SM 128x128 MMA needs 128),
+// and each SM loads only half of every K/V tile.
+//
+// Per CTA, tensor memory (512 columns x 128 lanes):
+//   cols [0,384)  three S/P buffers of 128 columns,  cols [384,512) O
+// Tile t uses buffer t % 3; its softmax output P (16-bit) overwrites the first
+// 64 columns of that buffer and is read by the TS-UMMA. With three buffers the
+// MMA warp keeps S up to three tiles ahead of the softmax warpgroup:
+//   per tile i:  once P(t_i) is ready, O += P(t_i) V(t_i), then S(t_{i+3})
+// into the buffer P(t_i) just left (UMMAs of one thread run in order).
+// K and V halves of a tile share one ring stage (one wait, one release).
+//
+// Warps per CTA: 0-3 softmax warpgroup (thread = query row), 4 MMA (the even
+// CTA's lane 0 issues; both CTAs' warp 4 allocate TMEM), 5 loads, 6-7 idle.
+// Barriers that collect both CTAs live in the even CTA; the even CTA's
+// commits are multicast to both. The (dynamic) unit index is broadcast by the
+// even CTA's load thread into both CTAs' unit rings.
+#pragma once
+#include "fmha_sm100.cuh"
+
+namespace chia {
+
+template <int D>
+struct Fmha2Config {
+  static_assert(D == 128, "the 2-SM kernel is specialised for head_dim 128");
+  static constexpr int BM = 128;  // query rows per CTA
+  static constexpr int BN = 128;  // keys per tile
+  static constexpr int Q_BYTES = BM * D * 2;          // 32 KB, two 128-byte chunks
+  static constexpr int Q_CHUNK = BM * 128;            // 16 KB
+  static constexpr int KH_ROWS = BN / 2;              // keys per CTA per K tile
+  static constexpr int KH_CHUNK = KH_ROWS * 128;      // 8 KB
+  static constexpr int HALF_BYTES = 16384;            // half a K or V tile
+  static constexpr int STAGE_BYTES = 2 * HALF_BYTES;  // [K half | V half] of one tile
+  static constexpr int NKV = 6;                       // ring stages (192 KB)
+  static constexpr int NSBUF = 3;                     // S/P buffers in TMEM
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_KV = OFF_Q + Q_BYTES;
+  static constexpr int OFF_BAR = OFF_KV + NKV * STAGE_BYTES;
+  // barriers (same offsets in both CTAs)
+  // even CTA only: q_full, kv_full[NKV], p_full, o_empty, unit_empty[2], drain
+  // both CTAs:     q_empty, kv_empty[NKV], s_full[2], pv_done, o_full, unit_full[2]
+  static constexpr int BAR_QFULL = 0;
+  static constexpr int BAR_QEMPTY = 1;
+  static constexpr int BAR_KVFULL = 2;
+  static constexpr int BAR_KVEMPTY = BAR_KVFULL + NKV;
+  static constexpr int BAR_SFULL = BAR_KVEMPTY + NKV;  // [NSBUF]
+  // P ready, per S/P buffer: one CTA's softmax may run up to two tiles ahead
+  // of the other's, so one barrier per buffer keeps the 8 arrivals of a phase
+  // from mixing tiles.
+  static constexpr int BAR_PFULL = BAR_SFULL + NSBUF;  // [NSBUF]
+  static constexpr int BAR_PVDONE = BAR_PFULL + NSBUF;
+  static constexpr int BAR_OFULL = BAR_PVDONE + 1;
+  static constexpr int BAR_OEMPTY = BAR_OFULL + 1;
+  static constexpr int BAR_UFULL = BAR_OEMPTY + 1;     // [2]
+  static constexpr int BAR_UEMPTY = BAR_UFULL + 2;     // [2]
+  static constexpr int BAR_DRAIN = BAR_UEMPTY + 2;
+  static constexpr int NUM_BARS = BAR_DRAIN + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // tmem base, abort, unit ring[2]
+  static constexpr int SMEM_BYTES = OFF_MISC + 16;
+  static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
+  static constexpr int THREADS = 256;
+  static constexpr int MMA_WARP = 4;
+  static constexpr int LOAD_WARP = 5;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t TMEM_O = 384;
+  static constexpr int UNIT_CONSUMERS = 1 + 4 + 4 + 1;  // MMA, 2 x softmax warps, odd loader
+  static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
+};
+
+// Per-kind constants of the softmax / pointwise epilogue.
+template <int KIND>
+__device__ __forceinline__ EpiConsts make_epi_consts(const KernelArgs &a, float hp) {
+  constexpr float LOG2E = 1.4426950408889634f;
+  EpiConsts kc;
+  kc.k_mul = a.score_scale * LOG2E;
+  kc.k_cap = 0.f;
+  kc.k_bias = 0.f;
+  kc.rel0 = 0.f;
+  if (KIND == KIND_SOFTMAX) kc.k_mul *= hp;
+  if (KIND == KIND_SOFTCAP) {
+    kc.k_mul = a.score_scale / a.softcap;
+    kc.k_cap = a.softcap * LOG2E;
+  }
+  if (KIND == KIND_ALIBI) kc.k_bias = hp * LOG2E * static_cast<float>(a.vdil);
+  if (KIND == KIND_SIGMOID) {
+    kc.k_mul = -a.score_scale * LOG2E;
+    kc.k_bias = -a.sig_bias * LOG2E;
+  }
+  if (KIND == KIND_RELU) kc.k_mul = a.score_scale;
+  return kc;
+}
+
+// Bounded wait on a local barrier that may receive arrivals from the other CTA.
+__device__ __forceinline__ bool bounded_wait_cl(const WaitCtx &c, uint32_t bar, uint32_t parity,
+                                                bool honour_abort = true) {
+  if (ptx::mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = ptx::globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (ptx::mbar_try_wait_cluster(bar, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (honour_abort && *c.abort) return false;
+      if (ptx::globaltimer_ns() - t0 > c.timeout_ns) {
+        *c.abort = 1;
+        if (c.status) atomicOr(c.status, 5 /* CHIA_ERR_DEVICE_TIMEOUT */);
+        return false;
+      }
+    }
+  }
+}
+
+template <int D, bool BF16, int KIND>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THREADS, 1)
+    fmha2_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
+                     const __grid_constant__ CUtensorMap tm_kh,
+                     const __grid_constant__ CUtensorMap tm_vh, const KernelArgs args) {
+  using C = Fmha2Config<D>;
+  constexpr int BM = C::BM, BN = C::BN, NKV = C::NKV;
+  constexpr bool SOFTMAX = (KIND == KIND_SOFTMAX || KIND == KIND_SOFTCAP || KIND == KIND_ALIBI);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = ptx::smem_u32(smem);
+  auto bar = [&](int idx) -> uint32_t { return sbase + C::OFF_BAR + idx * 8; };
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::OFF_MISC);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::OFF_MISC + 4);
+  volatile int *unit_ring = reinterpret_cast<volatile int *>(smem + C::OFF_MISC + 8);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = ptx::cluster_ctarank();
+  const bool leader = rank == 0;
+  const uint32_t pair = ptx::cluster_id_x(), npairs = ptx::cluster_count_x();
+  const MaskGeom &g = args.mask;
+  // address of barrier idx in the even CTA (shared::cluster window)
+  auto lbar = [&](int idx) -> uint32_t { return ptx::mapa(bar(idx), 0); };
+
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(bar(C::BAR_QFULL), 2);
+    ptx::mbar_init(bar(C::BAR_QEMPTY), 1);
+    for (int s = 0; s < NKV; ++s) {
+      ptx::mbar_init(bar(C::BAR_KVFULL + s), 2);
+      ptx::mbar_init(bar(C::BAR_KVEMPTY + s), 1);
+    }
+    for (int b = 0; b < C::NSBUF; ++b) {
+      ptx::mbar_init(bar(C::BAR_SFULL + b), 1);
+      ptx::mbar_init(bar(C::BAR_PFULL + b), 8);  // 4 softmax warps x 2 CTAs
+    }
+    ptx::mbar_init(bar(C::BAR_PVDONE), 1);
+    ptx::mbar_init(bar(C::BAR_OFULL), 1);
+    ptx::mbar_init(bar(C::BAR_OEMPTY), 8);  // 4 softmax warps x 2 CTAs
+    for (int s = 0; s < 2; ++s) {
+      ptx::mbar_init(bar(C::BAR_UFULL + s), 1);
+      ptx::mbar_init(bar(C::BAR_UEMPTY + s), C::UNIT_CONSUMERS);
+    }
+    ptx::mbar_init(bar(C::BAR_DRAIN), 1);
+    *abort_flag = 0;
+    ptx::fence_barrier_init();
+    ptx::fence_proxy_async_smem();
+  }
+  if (warp == C::LOAD_WARP && lane == 0) {
+    ptx::tma_prefetch_desc(&tm_q);
+    ptx::tma_prefetch_desc(&tm_kh);
+    ptx::tma_prefetch_desc(&tm_vh);
+  }
+  if (warp == C::MMA_WARP) {
+    ptx::tmem_alloc_2sm(ptx::smem_u32(tmem_slot), C::TMEM_COLS);
+    ptx::tmem_relinquish_2sm();
+  }
+  ptx::tc_fence_before();
+  ptx::cluster_sync();  // barriers of both CTAs initialised before any remote access
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const WaitCtx wc{abort_flag, args.status, args.timeout_ns};
+
+  if (warp == C::LOAD_WARP && lane == 0) {
+    // ========== unit scheduler (even CTA) + loads of this CTA's halves ==========
+    Tracer tr(3);
+    uint32_t n = 0;  // ring stages filled (one per tile)
+    int64_t last_item[NKV];
+    for (int s = 0; s < NKV; ++s) last_item[s] = -1;
+    // one tile: this CTA's K half (keys [64 rank, 64 rank + 64), two 64-column
+    // chunks) and V half (columns [64 rank, 64 rank + 64) of all 128 keys)
+    auto load_tile = [&](int64_t t, const UnitInfo &U) -> bool {
+      const int s = n % NKV;
+      if (!bounded_wait_cl(wc, bar(C::BAR_KVEMPTY + s), ((n / NKV) & 1) ^ 1)) return false;
+      const uint32_t full = lbar(C::BAR_KVFULL + s);
+      ptx::mbar_arrive_expect_tx_cluster(full, C::STAGE_BYTES);
+      const uint32_t dst = sbase + C::OFF_KV + s * C::STAGE_BYTES;
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c)
+        ptx::tma_load_5d_2sm(dst + c * C::KH_CHUNK, &tm_kh, full, c * 64,
+                             static_cast<int>(t * BN) + C::KH_ROWS * static_cast<int>(rank),
+                             U.r_res, U.h, U.b);
+      ptx::tma_load_5d_2sm(dst + C::HALF_BYTES, &tm_vh, full, 64 * static_cast<int>(rank),
+                           static_cast<int>(t * BN), U.r_res, U.h, U.b);
+      tr(30);
+      last_item[s] = n;
+      ++n;
+      return true;
+    };
+    for (int k = 0;; ++k) {
+      const int slot = k & 1;
+      int u;
+      if (leader) {
+        if (!bounded_wait_cl(wc, bar(C::BAR_UEMPTY + slot), ((k >> 1) & 1) ^ 1)) break;
+        u = args.sched ? atomicAdd(args.sched, 1)
+                       : static_cast<int>(pair) + k * static_cast<int>(npairs);
+        if (u >= args.n_units || u < 0) u = -1;
+        unit_ring[slot] = u;
+        ptx::st_shared_cluster_u32(ptx::mapa(sbase + C::OFF_MISC + 8 + 4 * slot, 1),
+                                   static_cast<uint32_t>(u));
+        ptx::mbar_arrive(bar(C::BAR_UFULL + slot));
+        ptx::mbar_arrive_cluster(ptx::mapa(bar(C::BAR_UFULL + slot), 1));
+      } else {
+        if (!bounded_wait_cl(wc, bar(C::BAR_UFULL + slot), (k >> 1) & 1)) break;
+        u = unit_ring[slot];
+        ptx::mbar_arrive_cluster(lbar(C::BAR_UEMPTY + slot));
+      }
+      if (u < 0) break;
+      UnitInfo U;
+      decode_unit<BM, BN>(u, args, U);
+      // this CTA's query tile (zero-filled by TMA when past the sequence end)
+      if (k > 0 && !bounded_wait_cl(wc, bar(C::BAR_QEMPTY), (k - 1) & 1)) break;
+      const uint32_t qfull = lbar(C::BAR_QFULL);
+      ptx::mbar_arrive_expect_tx_cluster(qfull, C::Q_BYTES);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c)
+        ptx::tma_load_5d_2sm(sbase + C::OFF_Q + c * C::Q_CHUNK, &tm_q, qfull, c * 64,
+                             static_cast<int>(U.m0) + BM * static_cast<int>(rank), U.r_res, U.h,
+                             U.b);
+      bool ok = true;
+      for (int64_t t = U.jlo; ok && t < U.jhi; ++t) ok = load_tile(t, U);
+      if (!ok) break;
+    }
+    // Drain: this CTA's copies have landed once the even CTA released their
+    // slots; on an abort the bounded waits below outlast any copy in flight.
+    for (int s = 0; s < NKV; ++s)
+      if (last_item[s] >= 0)
+        bounded_wait_cl(wc, bar(C::BAR_KVEMPTY + s), ((last_item[s] / NKV) & 1), false);
+  } else if (warp == C::MMA_WARP && lane == 0 && leader) {
+    // =========================== 2-SM UMMA issuer ===========================
+    constexpr uint32_t IDESC_QK = ptx::make_idesc_f16(2 * BM, BN, BF16, false, false);
+    constexpr uint32_t IDESC_PV = ptx::make_idesc_f16(2 * BM, D, BF16, false, true);
+    const uint32_t q_s = sbase + C::OFF_Q, kv_s = sbase + C::OFF_KV;
+    const uint64_t dq = ptx::make_sdesc_sw128(q_s, 16, 1024);
+    const uint64_t dk = ptx::make_sdesc_sw128(kv_s, 16, 1024);
+    const uint64_t dv = ptx::make_sdesc_sw128(kv_s + C::HALF_BYTES, C::HALF_BYTES, 1024);
+    constexpr uint16_t BOTH = 0x3;
+    auto issue_s = [&](uint32_t buf, int stage) {
+      const uint32_t d_tmem = tmem_base + buf * 128;
+      const uint64_t b0 = dk + ((stage * C::STAGE_BYTES) >> 4);
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        const uint32_t offq = ((kk >> 2) * C::Q_CHUNK + (kk & 3) * 32) >> 4;
+        const uint32_t offk = ((kk >> 2) * C::KH_CHUNK + (kk & 3) * 32) >> 4;
+        ptx::umma_ss_2sm(d_tmem, dq + offq, b0 + offk, IDESC_QK, kk > 0 ? 1u : 0u);
+      }
+    };
+    auto issue_pv = [&](uint32_t buf, int stage, bool first) {
+      const uint32_t d_tmem = tmem_base + C::TMEM_O;
+      const uint32_t p_tmem = tmem_base + buf * 128;
+      const uint64_t b0 = dv + ((stage * C::STAGE_BYTES) >> 4);
+#pragma unroll
+      for (int kk = 0; kk < BN / 16; ++kk)
+        ptx::umma_ts_2sm(d_tmem, p_tmem + kk * 8, b0 + ((kk * 2048) >> 4), IDESC_PV,
+                         (first && kk == 0) ? 0u : 1u);
+    };
+    Tracer tr(2);
+    uint32_t tcnt = 0;     // tiles issued = ring stage index = S/P buffer sequence
+    uint32_t units = 0;
+    bool ok = true;
+    auto stage_wait = [&](uint32_t t) {
+      return bounded_wait_cl(wc, bar(C::BAR_KVFULL + t % NKV), (t / NKV) & 1);
+    };
+    for (int k = 0; ok; ++k) {
+      const int slot = k & 1;
+      if (!bounded_wait_cl(wc, bar(C::BAR_UFULL + slot), (k >> 1) & 1)) break;
+      const int u = unit_ring[slot];
+      ptx::mbar_arrive(bar(C::BAR_UEMPTY + slot));
+      if (u < 0) break;
+      UnitInfo U;
+      decode_unit<BM, BN>(u, args, U);
+      if (!bounded_wait_cl(wc, bar(C::BAR_QFULL), k & 1)) break;
+      const int T = static_cast<int>(U.jhi - U.jlo);
+      // S of up to NSBUF tiles ahead
+      const int pre = T < C::NSBUF ? T : C::NSBUF;
+      for (int i = 0; i < pre; ++i) {
+        const uint32_t t = tcnt + i;
+        if (!stage_wait(t)) { ok = false; break; }
+        ptx::tc_fence_after();
+        issue_s(t % C::NSBUF, t % NKV);
+        ptx::umma_commit_2sm(bar(C::BAR_SFULL + t % C::NSBUF), BOTH);
+        tr(20);
+      }
+      if (!ok) break;
+      if (T <= C::NSBUF) ptx::umma_commit_2sm(bar(C::BAR_QEMPTY), BOTH);
+      for (int i = 0; i < T; ++i) {
+        const uint32_t t = tcnt + i, b = t % C::NSBUF;
+        if (!bounded_wait_cl(wc, bar(C::BAR_PFULL + b), (t / C::NSBUF) & 1)) { ok = false; break; }
+        tr(21);
+        if (i == 0 && units > 0 && !bounded_wait_cl(wc, bar(C::BAR_OEMPTY), (units - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        ptx::tc_fence_after();
+        issue_pv(b, t % NKV, i == 0);
+        ptx::umma_commit_2sm(bar(C::BAR_KVEMPTY + t % NKV), BOTH);  // K and V halves of tile t
+        if (SOFTMAX) ptx::umma_commit_2sm(bar(C::BAR_PVDONE), BOTH);
+        if (i == T - 1) ptx::umma_commit_2sm(bar(C::BAR_OFULL), BOTH);
+        tr(22);
+        if (i + C::NSBUF < T) {  // S three tiles ahead, into the buffer P(t) just left
+          const uint32_t t3 = t + C::NSBUF;
+          if (!stage_wait(t3)) { ok = false; break; }
+          ptx::tc_fence_after();
+          issue_s(b, t3 % NKV);
+          ptx::umma_commit_2sm(bar(C::BAR_SFULL + b), BOTH);
+          if (i + C::NSBUF == T - 1) ptx::umma_commit_2sm(bar(C::BAR_QEMPTY), BOTH);
+          tr(20);
+        }
+      }
+      if (!ok) break;
+      tcnt += T;
+      ++units;
+    }
+    ptx::umma_commit_2sm(bar(C::BAR_DRAIN), 0x1);  // every 2-SM UMMA of this thread retired
+    bounded_wait_cl(wc, bar(C::BAR_DRAIN), 0, false);
+  } else if (warp < 4) {
+    // ======================= softmax / epilogue =======================
+    const int row = warp * 32 + lane;  // TMEM lane = query row in this CTA's tile
+    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t tO = tmem_base + lane_off + C::TMEM_O;
+    const int prefix = static_cast<int>(g.prefix);
+    const int dil = static_cast<int>(g.dil);
+    const uint32_t pfull0 = lbar(C::BAR_PFULL), oempty = lbar(C::BAR_OEMPTY);
+    Tracer tr(warp == 0 ? 0 : 1);
+    const bool tracing = warp == 0 && lane == 0;
+    auto trs = [&](int tag) { if (tracing) tr(tag); };
+    uint32_t cnt = 0;  // tiles seen (all tiles of every unit)
+    uint32_t units = 0;
+    for (int k = 0;; ++k) {
+      const int slot = k & 1;
+      if (!bounded_wait_cl(wc, bar(C::BAR_UFULL + slot), (k >> 1) & 1)) break;
+      const int u = unit_ring[slot];
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive_cluster(lbar(C::BAR_UEMPTY + slot));
+      if (u < 0) break;
+      UnitInfo U;
+      decode_unit<BM, BN>(u, args, U);
+      const int w = static_cast<int>(rank);  // this CTA's query tile in the unit
+      const int i = static_cast<int>(U.m0) + w * BM + row;
+      const int64_t r0 = U.m0 + w * BM, r1 = r0 + BM - 1;
+      int64_t blo64, bhi64;
+      row_band(g, i, blo64, bhi64);
+      const bool band_empty = bhi64 < blo64;
+      const int blo = band_empty ? (1 << 30) : static_cast<int>(blo64);
+      const uint32_t span = band_empty ? 0u : static_cast<uint32_t>(bhi64 - blo64);
+      const float hp = args.head_param != nullptr ? args.head_param[U.h] : 1.0f;
+      EpiConsts kc = make_epi_consts<KIND>(args, hp);
+      float m_run = -INFINITY, l_run = 0.f;
+      bool ok = true, first_mine = true;
+      for (int64_t t = U.jlo; t < U.jhi; ++t, ++cnt) {
+        const uint32_t buf = cnt % C::NSBUF;
+        const uint32_t tS = tmem_base + lane_off + buf * 128;
+        if (!bounded_wait_cl(wc, bar(C::BAR_SFULL + buf), (cnt / C::NSBUF) & 1)) {
+          ok = false;
+          break;
+        }
+        trs(10);
+        ptx::tc_fence_after();
+        if (U.active(w, t)) {
+          uint32_t sr[4][32];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) ptx::tmem_ld32(tS + c * 32, sr[c]);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) ptx::reg_fence(sr[c]);
+          trs(11);
+          const int kv0 = static_cast<int>(t) * BN;
+          RowMask rm;
+          rm.c_lo = blo - kv0;
+          rm.span = span;
+          rm.c_pre = prefix - kv0;
+          rm.i_rel = i - kv0;
+          rm.dil = dil;
+          kc.rel0 = static_cast<float>(kv0 - i);
+          const int mode = tile_full(g, r0, r1, BN, t) ? 0 : (dil == 1 ? 1 : 2);
+          const PSinkTmem sink{tS};
+          if (SOFTMAX) {
+            float mx;
+            if (mode == 0)
+              mx = softmax_pass1<KIND, 0>(sr, kc, rm);
+            else if (mode == 1)
+              mx = softmax_pass1<KIND, 1>(sr, kc, rm);
+            else
+              mx = softmax_pass1<KIND, 2>(sr, kc, rm);
+            const float m_new = fmaxf(m_run, mx);
+            const bool need = m_new > m_run + 8.0f;
+            float alpha = 1.0f;
+            if (need) {
+              alpha = ptx::ex2(m_run - m_new);
+              l_run *= alpha;
+              m_run = m_new;
+            }
+            if (!first_mine && __any_sync(0xffffffffu, need)) {
+              // O holds every earlier PV once PV(t-1) retired
+              if (!bounded_wait_cl(wc, bar(C::BAR_PVDONE), (cnt - 1) & 1)) { ok = false; break; }
+              ptx::tc_fence_after();
+              rescale_rows<D>(tO, alpha);
+            }
+            const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
+            l_run += softmax_pass2<BF16>(sr, m_use, sink);
+          } else {
+            if (mode == 0)
+              pointwise_tile<KIND, 0, BF16>(sr, kc, rm, sink);
+            else if (mode == 1)
+              pointwise_tile<KIND, 1, BF16>(sr, kc, rm, sink);
+            else
+              pointwise_tile<KIND, 2, BF16>(sr, kc, rm, sink);
+          }
+          first_mine = false;
+          trs(12);
+        } else {
+          // the pair computes this tile for the other query tile only: P = 0 here
+          uint32_t z[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) z[e] = 0u;
+          ptx::tmem_st32(tS, z);
+          ptx::tmem_st32(tS + 32, z);
+        }
+        ptx::tmem_wait_st();
+        trs(16);  // P stores retired
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          if (leader)
+            ptx::mbar_arrive(bar(C::BAR_PFULL + buf));
+          else
+            ptx::mbar_arrive_cluster(pfull0 + 8 * buf);
+        }
+        trs(13);
+      }
+      if (!ok) break;
+      // ---------------- epilogue: O * inv -> global ----------------
+      if (!bounded_wait_cl(wc, bar(C::BAR_OFULL), units & 1)) break;
+      ptx::tc_fence_after();
+      float inv;
+      if (SOFTMAX)
+        inv = (l_run > 0.f) ? 1.0f / l_run : 0.f;
+      else if (KIND == KIND_RELU)
+        inv = args.out_scale;
+      else
+        inv = 1.0f;
+      const bool row_ok = U.wg_on(w) && i < g.sq;
+      const int64_t real_row = static_cast<int64_t>(i) * args.vdil + U.r_res;
+      uint8_t *orow = reinterpret_cast<uint8_t *>(args.o) +
+                      2 * (U.b * args.o_sb + static_cast<int64_t>(U.h) * args.o_sh +
+                           real_row * args.o_ss);
+      trs(14);
+      store_rows<D, BF16>(tO, inv, row_ok, orow);
+      trs(15);
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive_cluster(oempty);
+      ++units;
+    }
+  }
+
+  // ---- teardown: both CTAs finish before TMEM is freed and before either exits ----
+  __syncwarp();
+  ptx::tc_fence_before();
+  ptx::cluster_sync();
+  if (warp == C::MMA_WARP) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc_2sm(tmem_base, C::TMEM_COLS);
+  }
+  if (threadIdx.x == 0 && leader && args.sched != nullptr) {
+    __threadfence();
+    if (atomicAdd(args.sched + 1, 1) == static_cast<int>(npairs) - 1) {
+      atomicExch(args.sched, 0);
+      atomicExch(args.sched + 1, 0);
+    }
+  }
+}
+
+}  // namespace chia

@@ -266,16 +266,30 @@ __device__ __forceinline__ void store_p_chunk(uint32_t prow, int h2, int rsw,
                       pk[4 * u + 2], pk[4 * u + 3]);
 }
 
+// Destinations of a P row: 64 keys (32 packed pairs) at a time.
+struct PSinkSmem {  // shared-memory P tile (single-CTA kernel)
+  uint32_t prow;
+  int rsw;
+  __device__ __forceinline__ void operator()(int h2, const uint32_t (&pk)[32]) const {
+    store_p_chunk(prow, h2, rsw, pk);
+  }
+};
+struct PSinkTmem {  // TMEM columns of the S tile, read back by a TS-UMMA (2-SM kernel)
+  uint32_t tP;
+  __device__ __forceinline__ void operator()(int h2, const uint32_t (&pk)[32]) const {
+    ptx::tmem_st32(tP + h2 * 32, pk);
+  }
+};
+
 template <bool BF16>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return BF16 ? ptx::pack_bf16(lo, hi) : ptx::pack_f16(lo, hi);
 }
 
-// Softmax pass 2: p = 2^(x - m), packed to 16-bit pairs and written to this
-// row of the shared-memory P tile; returns the row sum of p.
-template <bool BF16>
-__device__ __forceinline__ float softmax_pass2(uint32_t (&sr)[4][32], float m, uint32_t prow,
-                                               int rsw) {
+// Softmax pass 2: p = 2^(x - m), packed to 16-bit pairs and handed to the
+// P sink 64 keys at a time; returns the row sum of p.
+template <bool BF16, class Sink>
+__device__ __forceinline__ float softmax_pass2(uint32_t (&sr)[4][32], float m, const Sink &sink) {
   const uint64_t NM2 = ptx::f2(-m, -m);
   uint64_t acc[2] = {ptx::f2(0.f, 0.f), ptx::f2(0.f, 0.f)};
 #pragma unroll
@@ -294,7 +308,7 @@ __device__ __forceinline__ float softmax_pass2(uint32_t (&sr)[4][32], float m, u
         pk[cc * 16 + e / 2] = pack2<BF16>(p0, p1);
       }
     }
-    store_p_chunk(prow, h2, rsw, pk);
+    sink(h2, pk);
   }
   float s0, s1, s2, s3;
   ptx::f2_split(acc[0], s0, s1);
@@ -303,14 +317,14 @@ __device__ __forceinline__ float softmax_pass2(uint32_t (&sr)[4][32], float m, u
 }
 
 // Non-softmax kinds: P = relu(s * scale) or sigmoid(s * scale + bias),
-// masked, packed and written to this row of the shared-memory P tile.
+// masked, packed and handed to the P sink.
 // Sigmoid is 1 / (1 + 2^t): 2^t on the MUFU, the reciprocal on the FMA pipe
 // (initial guess from the exponent-field complement 0x7EF311C7 - bits(y),
 // then two Newton steps r <- r (2 - y r); relative error about 2e-4, below
 // the 2^-9 rounding of the 16-bit P).
-template <int KIND, int MODE, bool BF16>
+template <int KIND, int MODE, bool BF16, class Sink>
 __device__ __forceinline__ void pointwise_tile(uint32_t (&sr)[4][32], const EpiConsts &k,
-                                               const RowMask &rm, uint32_t prow, int rsw) {
+                                               const RowMask &rm, const Sink &sink) {
   const uint64_t K2 = ptx::f2(k.k_mul, k.k_mul);
   const uint64_t KB2 = ptx::f2(k.k_bias, k.k_bias);
   const uint64_t NEG1 = ptx::f2(-1.0f, -1.0f);
@@ -354,7 +368,7 @@ __device__ __forceinline__ void pointwise_tile(uint32_t (&sr)[4][32], const EpiC
         }
       }
     }
-    store_p_chunk(prow, h2, rsw, pk);
+    sink(h2, pk);
   }
 }
 
@@ -823,15 +837,16 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
           }
           if (t > U.tlo[w] && __any_sync(0xffffffffu, need)) rescale_rows<D>(tO, alpha);
           const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-          l_run += softmax_pass2<BF16>(sr, m_use, prow, rsw);
+          l_run += softmax_pass2<BF16>(sr, m_use, PSinkSmem{prow, rsw});
         } else {
           if (cnt > 0 && !bounded_wait(wc, bar(C::BAR_PFREE + w), (cnt - 1) & 1)) { ok = false; break; }
+          const PSinkSmem sink{prow, rsw};
           if (mode == 0)
-            pointwise_tile<KIND, 0, BF16>(sr, kc, rm, prow, rsw);
+            pointwise_tile<KIND, 0, BF16>(sr, kc, rm, sink);
           else if (mode == 1)
-            pointwise_tile<KIND, 1, BF16>(sr, kc, rm, prow, rsw);
+            pointwise_tile<KIND, 1, BF16>(sr, kc, rm, sink);
           else
-            pointwise_tile<KIND, 2, BF16>(sr, kc, rm, prow, rsw);
+            pointwise_tile<KIND, 2, BF16>(sr, kc, rm, sink);
           trs(12);
         }
         ptx::tmem_wait_st();  // O rescale stores (rare)
