@@ -48,7 +48,7 @@ struct Fmha2Config {
   static constexpr int OFF_BAR = OFF_KV + NKV * STAGE_BYTES;
   // barriers (same offsets in both CTAs)
   // even CTA only: q_full, kv_full[NKV], p_full, o_empty, unit_empty[2], drain
-  // both CTAs:     q_empty, kv_empty[NKV], s_full[2], pv_done, o_full, unit_full[2]
+  // both CTAs:     q_empty, kv_empty[NKV], s_full[NSBUF], pv_done[2], o_full, unit_full[2]
   static constexpr int BAR_QFULL = 0;
   static constexpr int BAR_QEMPTY = 1;
   static constexpr int BAR_KVFULL = 2;
@@ -58,8 +58,12 @@ struct Fmha2Config {
   // of the other's, so one barrier per buffer keeps the 8 arrivals of a phase
   // from mixing tiles.
   static constexpr int BAR_PFULL = BAR_SFULL + NSBUF;  // [NSBUF]
-  static constexpr int BAR_PVDONE = BAR_PFULL + NSBUF;
-  static constexpr int BAR_OFULL = BAR_PVDONE + 1;
+  // PV(t) retired, alternating between two barriers by tile parity. A rescale
+  // at tile t waits for PV(t-1) while only PV(t-3) is known to have retired:
+  // with one barrier the wanted phase could be two behind, where a parity wait
+  // cannot tell it from the one before. On barrier (t-1) % 2 it is at most one.
+  static constexpr int BAR_PVDONE = BAR_PFULL + NSBUF;  // [2]
+  static constexpr int BAR_OFULL = BAR_PVDONE + 2;
   static constexpr int BAR_OEMPTY = BAR_OFULL + 1;
   static constexpr int BAR_UFULL = BAR_OEMPTY + 1;     // [2]
   static constexpr int BAR_UEMPTY = BAR_UFULL + 2;     // [2]
@@ -157,6 +161,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       ptx::mbar_init(bar(C::BAR_PFULL + b), 8);  // 4 softmax warps x 2 CTAs
     }
     ptx::mbar_init(bar(C::BAR_PVDONE), 1);
+    ptx::mbar_init(bar(C::BAR_PVDONE + 1), 1);
     ptx::mbar_init(bar(C::BAR_OFULL), 1);
     ptx::mbar_init(bar(C::BAR_OEMPTY), 8);  // 4 softmax warps x 2 CTAs
     for (int s = 0; s < 2; ++s) {
@@ -316,7 +321,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
         ptx::tc_fence_after();
         issue_pv(b, t % NKV, i == 0);
         ptx::umma_commit_2sm(bar(C::BAR_KVEMPTY + t % NKV), BOTH);  // K and V halves of tile t
-        if (SOFTMAX) ptx::umma_commit_2sm(bar(C::BAR_PVDONE), BOTH);
+        if (SOFTMAX) ptx::umma_commit_2sm(bar(C::BAR_PVDONE + (t & 1)), BOTH);
         if (i == T - 1) ptx::umma_commit_2sm(bar(C::BAR_OFULL), BOTH);
         tr(22);
         if (i + C::NSBUF < T) {  // S three tiles ahead, into the buffer P(t) just left
@@ -414,7 +419,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
             }
             if (!first_mine && __any_sync(0xffffffffu, need)) {
               // O holds every earlier PV once PV(t-1) retired
-              if (!bounded_wait_cl(wc, bar(C::BAR_PVDONE), (cnt - 1) & 1)) { ok = false; break; }
+              const uint32_t prev = cnt - 1;
+              if (!bounded_wait_cl(wc, bar(C::BAR_PVDONE + (prev & 1)), (prev >> 1) & 1)) {
+                ok = false;
+                break;
+              }
               ptx::tc_fence_after();
               rescale_rows<D>(tO, alpha);
             }

@@ -260,3 +260,25 @@ def test_static_and_dynamic_schedules_agree(cuda, op):
     assert torch.equal(a, b)
     torch.cuda.synchronize()
     assert int(ops._workspace(dev).abs().sum()) == 0
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("op,kw", [("bias_alibi", {}), ("softcap_gemma2", dict(cap=1000.0))])
+def test_running_max_rises_every_tile(cuda, op, D, kw):
+    """Scores grow along the keys by ~12 (log2 units) per 128-key tile, so the
+    running row maximum rises on every tile and O is rescaled on every tile
+    while earlier P.V products may still be in flight on the tensor core."""
+    B, H, S = 1, 4, 2048
+    g = torch.Generator().manual_seed(31)
+    q = torch.ones(B, H, S, D)
+    # score(i, j) = sqrt(D) * k_j: 8.7 nats = 12.5 log2 units more per 128 keys
+    ramp = torch.arange(S, dtype=torch.float32).view(1, 1, S, 1) * (8.7 / (128 * D ** 0.5))
+    k = ramp + 0.1 * torch.randn(B, H, S, D, generator=g)
+    v = torch.randn(B, H, S, D, generator=g)
+    q, k, v = (t.to(torch.bfloat16) for t in (q, k, v))
+    if op == "bias_alibi":
+        kw = dict(slopes=torch.zeros(H))
+    out = run(op, q, k, v, **kw)
+    check(out, oracle.run_op(op, q, k, v, **kw), op)
+    for _ in range(3):
+        assert torch.equal(out, run(op, q, k, v, **kw))
