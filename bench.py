@@ -68,6 +68,26 @@ def shard(units: int, ws: int, rank: int):
     return lo, hi
 
 
+def max_over_ranks(x: float, device, ws: int) -> float:
+    """The largest ``x`` over all ranks (every rank gets it)."""
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def gather_max(vals, device, ws: int):
+    """Element-wise maximum of the list ``vals`` over all ranks."""
+    e = torch.tensor(list(vals), dtype=torch.float64, device=device)
+    if ws > 1:
+        import torch.distributed as dist
+        gathered = [torch.zeros_like(e) for _ in range(ws)]
+        dist.all_gather(gathered, e)
+        e = torch.stack(gathered).max(0).values
+    return [float(x) for x in e]
+
+
 def variants():
     import chia_proj_b200 as cp
     return [
@@ -320,10 +340,7 @@ def run_ours(a):
                      for vi, (name, _, _) in enumerate(vs)}
     cp.check_device_status(local)
 
-    t = torch.tensor([ms], dtype=torch.float64, device=device)
-    if ws > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
+    ms_max = max_over_ranks(ms, device, ws)
     value = flops_step_total * a.steps / (ms_max * 1e-3) / 1e12
 
     # ---- verification: one unit per rank against an fp32 torch reference,
@@ -338,12 +355,8 @@ def run_ours(a):
             ref = p_ @ vf
             errs.append((outs[name][0, 0].float() - ref).abs().max().item())
             del s_, p_, ref
-    e = torch.tensor(errs, dtype=torch.float64, device=device)
-    if ws > 1:
-        gathered = [torch.zeros_like(e) for _ in range(ws)]
-        dist.all_gather(gathered, e)
-        e = torch.stack(gathered).max(0).values
-    verify = {name: float(e[i]) for i, (name, _, _) in enumerate(vs)}
+    e = gather_max(errs, device, ws)
+    verify = {name: e[i] for i, (name, _, _) in enumerate(vs)}
 
     # ---- end to end through the public API, host buffers, every step
     e2e = None
@@ -370,10 +383,7 @@ def run_ours(a):
         e1.record(stream)
         torch.cuda.synchronize()
         barrier()
-        t2 = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=device)
-        if ws > 1:
-            dist.all_reduce(t2, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t2.item())
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1), device, ws)
         bi = 3 * hq.numel() * hq.element_size()
         bo = len(vs) * hq.numel() * hq.element_size()
         e2e = {"value": round(flops_step_total * e2e_steps / (e2e_ms * 1e-3) / 1e12, 2),

@@ -9,7 +9,7 @@ reference's default parameters, and runs the sm_100a kernel of
 import os as _os
 import sys as _sys
 
-_ROOT = _os.path.dirname(_os.path.dirname(_os.path.dirname(_os.path.abspath(__file__))))
+_ROOT = _os.path.dirname(_os.path.dirname(_os.path.dirname(_os.path.realpath(__file__))))
 if _ROOT not in _sys.path:
     _sys.path.insert(0, _ROOT)
 

@@ -64,3 +64,28 @@ def test_plugin_runs_reference_shape(cuda, op):
     rel = (o - ref).abs().max().item() / (ref.abs().max().item() + 1e-6)
     assert rel < 3e-2, (op, rel)
     assert (o - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
+
+
+def test_plugins_load_from_a_reference_style_directory(lib, tmp_path):
+    """A reference checkout picks the plugins up from a ``kernels_gemini*``
+    directory of symlinks (``extra_bench.py:65-70``); loaded from there in a
+    fresh interpreter, each one still finds this package."""
+    import subprocess
+    import sys
+    d = tmp_path / "kernels_gemini_b200"
+    d.mkdir()
+    for p in glob.glob(os.path.join(PLUGINS, "*_BEST.py")):
+        os.symlink(p, d / os.path.basename(p))
+    prog = (
+        "import glob, importlib.util, os\n"
+        "n = 0\n"
+        "for p in glob.glob(os.path.join('kernels_gemini*', '*_BEST.py')):\n"
+        "    sp = importlib.util.spec_from_file_location('k' + str(abs(hash(p))), p)\n"
+        "    m = importlib.util.module_from_spec(sp); sp.loader.exec_module(m)\n"
+        "    assert callable(m.launch_kernel); n += 1\n"
+        "print(n)\n")
+    env = {k: v for k, v in os.environ.items() if k != "PYTHONPATH"}
+    out = subprocess.run([sys.executable, "-c", prog], cwd=tmp_path, env=env,
+                         capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr
+    assert out.stdout.strip() == str(len(cp.OPS))
