@@ -16,6 +16,8 @@ LIB_PATH = os.path.join(_HERE, "_lib", "libchia_attn.so")
 
 ABI_VERSION = 2
 WORKSPACE_BYTES = 256
+NOALLOC_SCRATCH_BYTES = 256
+NOALLOC_MAX_UNITS = 1 << 30
 
 DTYPE_BF16, DTYPE_F16 = 0, 1
 NORM_SOFTMAX, NORM_SIGMOID, NORM_RELU = 0, 1, 2
@@ -33,6 +35,7 @@ STATUS = {
 
 EXPORTED_SYMBOLS = (
     "chia_attn_fwd",
+    "chia_attn_fwd_noalloc",
     "chia_attn_visible_pairs",
     "chia_attn_tile_plan",
     "chia_attn_status_string",
@@ -104,6 +107,8 @@ def load() -> ctypes.CDLL:
             lib = ctypes.CDLL(LIB_PATH)
             lib.chia_attn_fwd.argtypes = [ctypes.POINTER(AttnParams), ctypes.c_void_p]
             lib.chia_attn_fwd.restype = ctypes.c_int
+            lib.chia_attn_fwd_noalloc.argtypes = [ctypes.POINTER(AttnParams), ctypes.c_void_p]
+            lib.chia_attn_fwd_noalloc.restype = ctypes.c_int
             lib.chia_attn_visible_pairs.argtypes = [ctypes.POINTER(AttnParams)]
             lib.chia_attn_visible_pairs.restype = ctypes.c_int64
             lib.chia_attn_tile_plan.argtypes = [

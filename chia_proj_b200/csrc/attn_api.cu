@@ -248,6 +248,35 @@ int kind_of(const chia_attn_params_t *p) {
   }
 }
 
+// ------------------------------------------------- library-owned scratch
+// Scheduler counters of chia_attn_fwd_noalloc: a file-scope device array, so
+// the entry point needs no allocation. In host code `g_noalloc_scratch` is a
+// stand-in for the device object, not an address; the device address is
+// looked up with cudaGetSymbolAddress once per device, with it current.
+static_assert(CHIA_ATTN_NOALLOC_SCRATCH_BYTES >= CHIA_ATTN_WORKSPACE_BYTES,
+              "scratch must hold the scheduler workspace");
+static __device__ __align__(256) int32_t g_noalloc_scratch[CHIA_ATTN_NOALLOC_SCRATCH_BYTES / 4];
+
+constexpr int kMaxDevices = 64;
+std::atomic<void *> g_noalloc_addr[kMaxDevices];
+std::mutex g_noalloc_mutex;
+
+int noalloc_scratch_addr(int dev, void **out) {
+  if (dev < 0 || dev >= kMaxDevices) return CHIA_ERR_UNSUPPORTED;
+  void *ptr = g_noalloc_addr[dev].load(std::memory_order_acquire);
+  if (ptr == nullptr) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    ptr = g_noalloc_addr[dev].load(std::memory_order_acquire);
+    if (ptr == nullptr) {
+      if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr)
+        return CHIA_ERR_LAUNCH;
+      g_noalloc_addr[dev].store(ptr, std::memory_order_release);
+    }
+  }
+  *out = ptr;
+  return CHIA_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -368,6 +397,32 @@ int chia_attn_fwd(const chia_attn_params_t *p, void *stream) {
   }
   return bf16 ? launch_kind<64, true>(kind, mq, mk, mv, a, nblocks, s)
               : launch_kind<64, false>(kind, mq, mk, mv, a, nblocks, s);
+}
+
+int chia_attn_fwd_noalloc(const chia_attn_params_t *p, void *stream) {
+  const int v = validate(p);
+  if (v != CHIA_OK) return v;
+  if (p->workspace != nullptr) return CHIA_ERR_INVALID_ARGUMENT;
+  Derived dv;
+  derive(p, dv);
+  const int64_t units = (dv.geom.sq + 255) / 256 * p->batch * p->heads * dv.vdil;
+  if (units > CHIA_ATTN_NOALLOC_MAX_UNITS) return CHIA_ERR_UNSUPPORTED;
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHIA_ERR_NO_DEVICE;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      major != 10)
+    return CHIA_ERR_NO_DEVICE;
+  void *scratch = nullptr;
+  const int r = noalloc_scratch_addr(dev, &scratch);
+  if (r != CHIA_OK) return r;
+  // The counters must start at zero; a call that ended early (device timeout)
+  // may have left them set, so clear them on the stream before every launch.
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (cudaMemsetAsync(scratch, 0, CHIA_ATTN_WORKSPACE_BYTES, s) != cudaSuccess)
+    return CHIA_ERR_LAUNCH;
+  chia_attn_params_t q = *p;
+  q.workspace = scratch;
+  return chia_attn_fwd(&q, stream);
 }
 
 }  // extern "C"

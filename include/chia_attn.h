@@ -147,6 +147,32 @@ typedef struct chia_attn_params {
  * errors are reported before anything is launched. */
 CHIA_API int chia_attn_fwd(const chia_attn_params_t *params, void *stream);
 
+/* Size of the library-owned scratch used by chia_attn_fwd_noalloc, and the
+ * largest problem it accepts, counted in work units of 256 query rows of one
+ * (batch, head) pair: ceil(seqlen_q / 256) * batch * heads (times dilation
+ * when seqlen_q and seqlen_kv are multiples of it and block == prefix == 0). */
+#define CHIA_ATTN_NOALLOC_SCRATCH_BYTES 256
+#define CHIA_ATTN_NOALLOC_MAX_UNITS (1 << 30)
+
+/* chia_attn_fwd for callers that cannot allocate device memory. No
+ * counterpart in the reference: its launch_kernel(q, k, v) allocates its own
+ * output with torch. A plugin host or FFI caller that owns all device memory
+ * and keeps no per-device state between calls has nowhere to keep the
+ * scheduler workspace, and cudaMalloc on every call would synchronise the
+ * device. This entry point takes params->workspace == NULL (anything else is
+ * CHIA_ERR_INVALID_ARGUMENT) and schedules with a file-scope device array of
+ * CHIA_ATTN_NOALLOC_SCRATCH_BYTES instead, which every GPU that loads the
+ * library holds until the process exits. It calls no cudaMalloc, cudaFree or
+ * other allocating routine; it zeroes the array on `stream` before the
+ * launch. Problems of more than CHIA_ATTN_NOALLOC_MAX_UNITS work units return
+ * CHIA_ERR_UNSUPPORTED before anything is enqueued. The first call on a
+ * device looks up the array's device address (with that device current), so
+ * make that first call before any stream capture. All calls on one device
+ * share the array: calls that overlap on the GPU (different streams, no
+ * ordering between them) race on it and may compute wrong outputs. Inputs,
+ * output, status and all other fields are as for chia_attn_fwd. */
+CHIA_API int chia_attn_fwd_noalloc(const chia_attn_params_t *params, void *stream);
+
 /* Number of visible (i, j) pairs of the mask described by params for one
  * (batch, head) pair -- the mask-aware FLOP count is 4 * D * pairs * B * H.
  * Host-only integer arithmetic; needs no GPU. Returns -1 on bad params. */
