@@ -13,15 +13,22 @@
 //
 // Per CTA, tensor memory (512 columns x 128 lanes):
 //   cols [0,384)  three S/P buffers of 128 columns,  cols [384,512) O
-// Tile t uses buffer t % 3; its softmax output P (16-bit) overwrites the first
-// 64 columns of that buffer and is read by the TS-UMMA. With three buffers the
-// MMA warp keeps S up to three tiles ahead of the softmax warpgroup:
+// Tile t uses buffer t % 3. Its softmax output P (16-bit pairs) overwrites
+// columns [0,32) (keys 0-63) and [64,96) (keys 64-127) of that buffer, each
+// half inside the S columns of the warpgroup that wrote it, and is read back
+// by the TS-UMMA. With three buffers the MMA warp keeps S up to three tiles
+// ahead of the softmax warpgroups:
 //   per tile i:  once P(t_i) is ready, O += P(t_i) V(t_i), then S(t_{i+3})
 // into the buffer P(t_i) just left (UMMAs of one thread run in order).
 // K and V halves of a tile share one ring stage (one wait, one release).
 //
-// Warps per CTA: 0-3 softmax warpgroup (thread = query row), 4 MMA (the even
-// CTA's lane 0 issues; both CTAs' warp 4 allocate TMEM), 5 loads, 6-7 idle.
+// Warps per CTA: 0-7 two softmax warpgroups; warp w owns TMEM lanes (query
+// rows) 32 (w % 4) .. +31 and key columns 64 (w / 4) .. +63 of every tile, so
+// each thread transforms half a row. Softmax kinds combine the two halves'
+// row maxima through shared memory once per tile (64-thread named barrier per
+// lane quadrant) and the row sums once per unit; each warpgroup rescales and
+// stores its own 64 columns of O. Warp 8 issues MMAs (the even CTA's lane 0;
+// both CTAs' warp 8 allocate TMEM), warp 9 loads.
 // Barriers that collect both CTAs live in the even CTA; the even CTA's
 // commits are multicast to both. The (dynamic) unit index is broadcast by the
 // even CTA's load thread into both CTAs' unit rings.
@@ -41,7 +48,7 @@ struct Fmha2Config {
   static constexpr int KH_CHUNK = KH_ROWS * 128;      // 8 KB
   static constexpr int HALF_BYTES = 16384;            // half a K or V tile
   static constexpr int STAGE_BYTES = 2 * HALF_BYTES;  // [K half | V half] of one tile
-  static constexpr int NKV = 6;                       // ring stages (192 KB)
+  static constexpr int NKV = 5;                       // ring stages (160 KB)
   static constexpr int NSBUF = 3;                     // S/P buffers in TMEM
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_KV = OFF_Q + Q_BYTES;
@@ -68,16 +75,22 @@ struct Fmha2Config {
   static constexpr int BAR_UFULL = BAR_OEMPTY + 1;     // [2]
   static constexpr int BAR_UEMPTY = BAR_UFULL + 2;     // [2]
   static constexpr int BAR_DRAIN = BAR_UEMPTY + 2;
-  static constexpr int NUM_BARS = BAR_DRAIN + 1;
+  // exchange between the two softmax warps of one lane quadrant: [4 quad][2 slot]
+  static constexpr int BAR_XCH = BAR_DRAIN + 1;
+  static constexpr int NUM_BARS = BAR_XCH + 8;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // tmem base, abort, unit ring[2]
-  static constexpr int SMEM_BYTES = OFF_MISC + 16;
+  // row-max / row-sum exchange between the two softmax warpgroups:
+  // float [2 parity][2 column half][128 rows]
+  static constexpr int OFF_XCH = OFF_MISC + 16;
+  static constexpr int SMEM_BYTES = OFF_XCH + 2 * 2 * 128 * 4;
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
-  static constexpr int THREADS = 256;
-  static constexpr int MMA_WARP = 4;
-  static constexpr int LOAD_WARP = 5;
+  static constexpr int THREADS = 320;
+  static constexpr int SOFTMAX_WARPS = 8;
+  static constexpr int MMA_WARP = 8;
+  static constexpr int LOAD_WARP = 9;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t TMEM_O = 384;
-  static constexpr int UNIT_CONSUMERS = 1 + 4 + 4 + 1;  // MMA, 2 x softmax warps, odd loader
+  static constexpr int UNIT_CONSUMERS = 1 + 8 + 8 + 1;  // MMA, 2 x softmax warps, odd loader
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
 };
 
@@ -158,17 +171,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
     }
     for (int b = 0; b < C::NSBUF; ++b) {
       ptx::mbar_init(bar(C::BAR_SFULL + b), 1);
-      ptx::mbar_init(bar(C::BAR_PFULL + b), 8);  // 4 softmax warps x 2 CTAs
+      ptx::mbar_init(bar(C::BAR_PFULL + b), 2 * C::SOFTMAX_WARPS);  // both CTAs
     }
     ptx::mbar_init(bar(C::BAR_PVDONE), 1);
     ptx::mbar_init(bar(C::BAR_PVDONE + 1), 1);
     ptx::mbar_init(bar(C::BAR_OFULL), 1);
-    ptx::mbar_init(bar(C::BAR_OEMPTY), 8);  // 4 softmax warps x 2 CTAs
+    ptx::mbar_init(bar(C::BAR_OEMPTY), 2 * C::SOFTMAX_WARPS);  // both CTAs
     for (int s = 0; s < 2; ++s) {
       ptx::mbar_init(bar(C::BAR_UFULL + s), 1);
       ptx::mbar_init(bar(C::BAR_UEMPTY + s), C::UNIT_CONSUMERS);
     }
     ptx::mbar_init(bar(C::BAR_DRAIN), 1);
+    for (int x = 0; x < 8; ++x) ptx::mbar_init(bar(C::BAR_XCH + x), 2);  // one arrive per warp
     *abort_flag = 0;
     ptx::fence_barrier_init();
     ptx::fence_proxy_async_smem();
@@ -198,9 +212,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
     // chunks) and V half (columns [64 rank, 64 rank + 64) of all 128 keys)
     auto load_tile = [&](int64_t t, const UnitInfo &U) -> bool {
       const int s = n % NKV;
-      if (!bounded_wait_cl(wc, bar(C::BAR_KVEMPTY + s), ((n / NKV) & 1) ^ 1)) return false;
+      if (!bounded_wait(wc, bar(C::BAR_KVEMPTY + s), ((n / NKV) & 1) ^ 1)) return false;
       const uint32_t full = lbar(C::BAR_KVFULL + s);
-      ptx::mbar_arrive_expect_tx_cluster(full, C::STAGE_BYTES);
+      ptx::mbar_arrive_expect_tx_remote(full, C::STAGE_BYTES);
       const uint32_t dst = sbase + C::OFF_KV + s * C::STAGE_BYTES;
 #pragma unroll
       for (int c = 0; c < D / 64; ++c)
@@ -236,9 +250,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       UnitInfo U;
       decode_unit<BM, BN>(u, args, U);
       // this CTA's query tile (zero-filled by TMA when past the sequence end)
-      if (k > 0 && !bounded_wait_cl(wc, bar(C::BAR_QEMPTY), (k - 1) & 1)) break;
+      if (k > 0 && !bounded_wait(wc, bar(C::BAR_QEMPTY), (k - 1) & 1)) break;
       const uint32_t qfull = lbar(C::BAR_QFULL);
-      ptx::mbar_arrive_expect_tx_cluster(qfull, C::Q_BYTES);
+      ptx::mbar_arrive_expect_tx_remote(qfull, C::Q_BYTES);
 #pragma unroll
       for (int c = 0; c < D / 64; ++c)
         ptx::tma_load_5d_2sm(sbase + C::OFF_Q + c * C::Q_CHUNK, &tm_q, qfull, c * 64,
@@ -252,7 +266,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
     // slots; on an abort the bounded waits below outlast any copy in flight.
     for (int s = 0; s < NKV; ++s)
       if (last_item[s] >= 0)
-        bounded_wait_cl(wc, bar(C::BAR_KVEMPTY + s), ((last_item[s] / NKV) & 1), false);
+        bounded_wait(wc, bar(C::BAR_KVEMPTY + s), ((last_item[s] / NKV) & 1), false);
   } else if (warp == C::MMA_WARP && lane == 0 && leader) {
     // =========================== 2-SM UMMA issuer ===========================
     constexpr uint32_t IDESC_QK = ptx::make_idesc_f16(2 * BM, BN, BF16, false, false);
@@ -277,16 +291,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       const uint32_t p_tmem = tmem_base + buf * 128;
       const uint64_t b0 = dv + ((stage * C::STAGE_BYTES) >> 4);
 #pragma unroll
-      for (int kk = 0; kk < BN / 16; ++kk)
-        ptx::umma_ts_2sm(d_tmem, p_tmem + kk * 8, b0 + ((kk * 2048) >> 4), IDESC_PV,
-                         (first && kk == 0) ? 0u : 1u);
+      for (int kk = 0; kk < BN / 16; ++kk)  // P of keys 16kk.. at column 8kk (+32 past key 64)
+        ptx::umma_ts_2sm(d_tmem, p_tmem + kk * 8 + (kk >= 4 ? 32 : 0), b0 + ((kk * 2048) >> 4),
+                         IDESC_PV, (first && kk == 0) ? 0u : 1u);
     };
     Tracer tr(2);
     uint32_t tcnt = 0;     // tiles issued = ring stage index = S/P buffer sequence
     uint32_t units = 0;
     bool ok = true;
     auto stage_wait = [&](uint32_t t) {
-      return bounded_wait_cl(wc, bar(C::BAR_KVFULL + t % NKV), (t / NKV) & 1);
+      return bounded_wait(wc, bar(C::BAR_KVFULL + t % NKV), (t / NKV) & 1);
     };
     for (int k = 0; ok; ++k) {
       const int slot = k & 1;
@@ -296,7 +310,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       if (u < 0) break;
       UnitInfo U;
       decode_unit<BM, BN>(u, args, U);
-      if (!bounded_wait_cl(wc, bar(C::BAR_QFULL), k & 1)) break;
+      if (!bounded_wait(wc, bar(C::BAR_QFULL), k & 1)) break;
       const int T = static_cast<int>(U.jhi - U.jlo);
       // S of up to NSBUF tiles ahead
       const int pre = T < C::NSBUF ? T : C::NSBUF;
@@ -312,9 +326,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       if (T <= C::NSBUF) ptx::umma_commit_2sm(bar(C::BAR_QEMPTY), BOTH);
       for (int i = 0; i < T; ++i) {
         const uint32_t t = tcnt + i, b = t % C::NSBUF;
-        if (!bounded_wait_cl(wc, bar(C::BAR_PFULL + b), (t / C::NSBUF) & 1)) { ok = false; break; }
+        if (!bounded_wait(wc, bar(C::BAR_PFULL + b), (t / C::NSBUF) & 1)) { ok = false; break; }
         tr(21);
-        if (i == 0 && units > 0 && !bounded_wait_cl(wc, bar(C::BAR_OEMPTY), (units - 1) & 1)) {
+        if (i == 0 && units > 0 && !bounded_wait(wc, bar(C::BAR_OEMPTY), (units - 1) & 1)) {
           ok = false;
           break;
         }
@@ -339,15 +353,34 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       ++units;
     }
     ptx::umma_commit_2sm(bar(C::BAR_DRAIN), 0x1);  // every 2-SM UMMA of this thread retired
-    bounded_wait_cl(wc, bar(C::BAR_DRAIN), 0, false);
-  } else if (warp < 4) {
+    bounded_wait(wc, bar(C::BAR_DRAIN), 0, false);
+  } else if (warp < C::SOFTMAX_WARPS) {
     // ======================= softmax / epilogue =======================
-    const int row = warp * 32 + lane;  // TMEM lane = query row in this CTA's tile
-    const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
-    const uint32_t tO = tmem_base + lane_off + C::TMEM_O;
+    const int quad = warp & 3, half = warp >> 2;
+    const int row = quad * 32 + lane;  // TMEM lane = query row in this CTA's tile
+    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t tO = tmem_base + lane_off + C::TMEM_O + half * 64;
     const int prefix = static_cast<int>(g.prefix);
     const int dil = static_cast<int>(g.dil);
     const uint32_t pfull0 = lbar(C::BAR_PFULL), oempty = lbar(C::BAR_OEMPTY);
+    float *xch = reinterpret_cast<float *>(smem + C::OFF_XCH);
+    uint32_t xcnt = 0;
+    // Hands v to the warp that owns the other column half of these rows and
+    // returns its value in `other`. Both warps call it in the same order; two
+    // slots keep a fast warp from overwriting a value the other has not read
+    // (it cannot reach exchange n+2 before the other arrived at n+1). The
+    // wait is bounded: false means the kernel is aborting.
+    auto exchange = [&](float v, float &other) -> bool {
+      const uint32_t slot = xcnt & 1, phase = (xcnt >> 1) & 1;
+      ++xcnt;
+      xch[slot * 256 + half * 128 + row] = v;
+      __syncwarp();
+      const uint32_t xb = bar(C::BAR_XCH + quad * 2 + slot);
+      if (lane == 0) ptx::mbar_arrive(xb);
+      if (!bounded_wait(wc, xb, phase)) return false;
+      other = xch[slot * 256 + (half ^ 1) * 128 + row];
+      return true;
+    };
     Tracer tr(warp == 0 ? 0 : 1);
     const bool tracing = warp == 0 && lane == 0;
     auto trs = [&](int tag) { if (tracing) tr(tag); };
@@ -376,22 +409,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       bool ok = true, first_mine = true;
       for (int64_t t = U.jlo; t < U.jhi; ++t, ++cnt) {
         const uint32_t buf = cnt % C::NSBUF;
-        const uint32_t tS = tmem_base + lane_off + buf * 128;
-        if (!bounded_wait_cl(wc, bar(C::BAR_SFULL + buf), (cnt / C::NSBUF) & 1)) {
+        const uint32_t tS = tmem_base + lane_off + buf * 128 + half * 64;
+        if (!bounded_wait(wc, bar(C::BAR_SFULL + buf), (cnt / C::NSBUF) & 1)) {
           ok = false;
           break;
         }
         trs(10);
         ptx::tc_fence_after();
         if (U.active(w, t)) {
-          uint32_t sr[4][32];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) ptx::tmem_ld32(tS + c * 32, sr[c]);
+          uint32_t sr[2][32];
+          ptx::tmem_ld32(tS, sr[0]);
+          ptx::tmem_ld32(tS + 32, sr[1]);
           ptx::tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 4; ++c) ptx::reg_fence(sr[c]);
+          ptx::reg_fence(sr[0]);
+          ptx::reg_fence(sr[1]);
           trs(11);
-          const int kv0 = static_cast<int>(t) * BN;
+          const int kv0 = static_cast<int>(t) * BN + half * 64;  // key of column 0 of sr
           RowMask rm;
           rm.c_lo = blo - kv0;
           rm.span = span;
@@ -400,7 +433,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
           rm.dil = dil;
           kc.rel0 = static_cast<float>(kv0 - i);
           const int mode = tile_full(g, r0, r1, BN, t) ? 0 : (dil == 1 ? 1 : 2);
-          const PSinkTmem sink{tS};
+          const PSinkTmem sink{tS};  // P of these 64 keys -> first 32 of these columns
           if (SOFTMAX) {
             float mx;
             if (mode == 0)
@@ -409,6 +442,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
               mx = softmax_pass1<KIND, 1>(sr, kc, rm);
             else
               mx = softmax_pass1<KIND, 2>(sr, kc, rm);
+            float mx_other;
+            if (!exchange(mx, mx_other)) { ok = false; break; }
+            mx = fmaxf(mx, mx_other);  // row maximum over the whole tile
             const float m_new = fmaxf(m_run, mx);
             const bool need = m_new > m_run + 8.0f;
             float alpha = 1.0f;
@@ -420,12 +456,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
             if (!first_mine && __any_sync(0xffffffffu, need)) {
               // O holds every earlier PV once PV(t-1) retired
               const uint32_t prev = cnt - 1;
-              if (!bounded_wait_cl(wc, bar(C::BAR_PVDONE + (prev & 1)), (prev >> 1) & 1)) {
+              if (!bounded_wait(wc, bar(C::BAR_PVDONE + (prev & 1)), (prev >> 1) & 1)) {
                 ok = false;
                 break;
               }
               ptx::tc_fence_after();
-              rescale_rows<D>(tO, alpha);
+              rescale_rows<64>(tO, alpha);
             }
             const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
             l_run += softmax_pass2<BF16>(sr, m_use, sink);
@@ -445,7 +481,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
 #pragma unroll
           for (int e = 0; e < 32; ++e) z[e] = 0u;
           ptx::tmem_st32(tS, z);
-          ptx::tmem_st32(tS + 32, z);
         }
         ptx::tmem_wait_st();
         trs(16);  // P stores retired
@@ -455,32 +490,36 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
           if (leader)
             ptx::mbar_arrive(bar(C::BAR_PFULL + buf));
           else
-            ptx::mbar_arrive_cluster(pfull0 + 8 * buf);
+            ptx::mbar_arrive_remote(pfull0 + 8 * buf);
         }
         trs(13);
       }
       if (!ok) break;
       // ---------------- epilogue: O * inv -> global ----------------
-      if (!bounded_wait_cl(wc, bar(C::BAR_OFULL), units & 1)) break;
-      ptx::tc_fence_after();
       float inv;
-      if (SOFTMAX)
-        inv = (l_run > 0.f) ? 1.0f / l_run : 0.f;
-      else if (KIND == KIND_RELU)
+      if (SOFTMAX) {
+        float l_other;
+        if (!exchange(l_run, l_other)) break;
+        const float l_tot = l_run + l_other;
+        inv = (l_tot > 0.f) ? 1.0f / l_tot : 0.f;
+      } else if (KIND == KIND_RELU) {
         inv = args.out_scale;
-      else
+      } else {
         inv = 1.0f;
+      }
+      if (!bounded_wait(wc, bar(C::BAR_OFULL), units & 1)) break;
+      ptx::tc_fence_after();
       const bool row_ok = U.wg_on(w) && i < g.sq;
       const int64_t real_row = static_cast<int64_t>(i) * args.vdil + U.r_res;
       uint8_t *orow = reinterpret_cast<uint8_t *>(args.o) +
                       2 * (U.b * args.o_sb + static_cast<int64_t>(U.h) * args.o_sh +
-                           real_row * args.o_ss);
+                           real_row * args.o_ss + half * 64);
       trs(14);
-      store_rows<D, BF16>(tO, inv, row_ok, orow);
+      store_rows<64, BF16>(tO, inv, row_ok, orow);
       trs(15);
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive_cluster(oempty);
+      if (lane == 0) ptx::mbar_arrive_remote(oempty);
       ++units;
     }
   }

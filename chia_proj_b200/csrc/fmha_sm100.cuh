@@ -215,16 +215,18 @@ __device__ __forceinline__ bool col_visible(const RowMask &rm, int col) {
 // Softmax kinds, pass 1: score -> log2-domain logit x (modified and masked)
 // in place; returns the row maximum. Work is done on packed pairs of columns.
 // MODE 0: tile fully visible (no mask code); 1: band + prefix; 2: + dilation.
-template <int KIND, int MODE>
-__device__ __forceinline__ float softmax_pass1(uint32_t (&sr)[4][32], const EpiConsts &k,
+// NC chunks of 32 columns; EpiConsts::rel0 and RowMask refer to column 0 of
+// sr, so a thread may own any 32-column-aligned part of the tile.
+template <int KIND, int MODE, int NC = 4>
+__device__ __forceinline__ float softmax_pass1(uint32_t (&sr)[NC][32], const EpiConsts &k,
                                                const RowMask &rm) {
   const uint64_t K2 = ptx::f2(k.k_mul, k.k_mul);
   const uint64_t CAP2 = ptx::f2(k.k_cap, k.k_cap);
   const uint64_t KB2 = ptx::f2(k.k_bias, k.k_bias);
   const uint64_t REL2 = ptx::f2(k.rel0, k.rel0 + 1.0f);
-  float m[4];
+  float m[NC];
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < NC; ++c) {
     float mc = -INFINITY;
 #pragma unroll
     for (int e = 0; e < 32; e += 2) {
@@ -251,7 +253,11 @@ __device__ __forceinline__ float softmax_pass1(uint32_t (&sr)[4][32], const EpiC
     }
     m[c] = mc;
   }
-  return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+  static_assert(NC == 2 || NC == 4, "64 or 128 columns");
+  if constexpr (NC == 4)
+    return fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3]));
+  else
+    return fmaxf(m[0], m[1]);
 }
 
 // Write 64 keys (32 packed pairs) of this thread's P row into the
@@ -288,12 +294,13 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
 
 // Softmax pass 2: p = 2^(x - m), packed to 16-bit pairs and handed to the
 // P sink 64 keys at a time; returns the row sum of p.
-template <bool BF16, class Sink>
-__device__ __forceinline__ float softmax_pass2(uint32_t (&sr)[4][32], float m, const Sink &sink) {
+template <bool BF16, class Sink, int NC = 4>
+__device__ __forceinline__ float softmax_pass2(uint32_t (&sr)[NC][32], float m, const Sink &sink) {
+  static_assert(NC == 2 || NC == 4, "64 or 128 columns");
   const uint64_t NM2 = ptx::f2(-m, -m);
   uint64_t acc[2] = {ptx::f2(0.f, 0.f), ptx::f2(0.f, 0.f)};
 #pragma unroll
-  for (int h2 = 0; h2 < 2; ++h2) {
+  for (int h2 = 0; h2 < NC / 2; ++h2) {
     uint32_t pk[32];
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
@@ -322,15 +329,16 @@ __device__ __forceinline__ float softmax_pass2(uint32_t (&sr)[4][32], float m, c
 // (initial guess from the exponent-field complement 0x7EF311C7 - bits(y),
 // then two Newton steps r <- r (2 - y r); relative error about 2e-4, below
 // the 2^-9 rounding of the 16-bit P).
-template <int KIND, int MODE, bool BF16, class Sink>
-__device__ __forceinline__ void pointwise_tile(uint32_t (&sr)[4][32], const EpiConsts &k,
+template <int KIND, int MODE, bool BF16, class Sink, int NC = 4>
+__device__ __forceinline__ void pointwise_tile(uint32_t (&sr)[NC][32], const EpiConsts &k,
                                                const RowMask &rm, const Sink &sink) {
+  static_assert(NC == 2 || NC == 4, "64 or 128 columns");
   const uint64_t K2 = ptx::f2(k.k_mul, k.k_mul);
   const uint64_t KB2 = ptx::f2(k.k_bias, k.k_bias);
   const uint64_t NEG1 = ptx::f2(-1.0f, -1.0f);
   const uint64_t TWO2 = ptx::f2(2.0f, 2.0f);
 #pragma unroll
-  for (int h2 = 0; h2 < 2; ++h2) {
+  for (int h2 = 0; h2 < NC / 2; ++h2) {
     uint32_t pk[32];
 #pragma unroll
     for (int cc = 0; cc < 2; ++cc) {
@@ -372,7 +380,8 @@ __device__ __forceinline__ void pointwise_tile(uint32_t (&sr)[4][32], const EpiC
   }
 }
 
-// O_w rows of this warp *= alpha (lazy softmax rescale; rare).
+// D columns of O (from tO) of this thread's row *= alpha (lazy softmax
+// rescale; rare).
 template <int D>
 __device__ __noinline__ void rescale_rows(uint32_t tO, float alpha) {
 #pragma unroll 1
@@ -387,7 +396,8 @@ __device__ __noinline__ void rescale_rows(uint32_t tO, float alpha) {
   }
 }
 
-// Epilogue: O row * inv -> 16-bit -> global (one thread per row).
+// Epilogue: D columns of O row (from tO) * inv -> 16-bit -> global at orow
+// (one thread per row).
 template <int D, bool BF16>
 __device__ __forceinline__ void store_rows(uint32_t tO, float inv, bool row_ok, uint8_t *orow) {
 #pragma unroll 1
