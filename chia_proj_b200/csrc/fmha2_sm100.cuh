@@ -55,7 +55,7 @@ struct Fmha2Config {
   static constexpr int OFF_BAR = OFF_KV + NKV * STAGE_BYTES;
   // barriers (same offsets in both CTAs)
   // even CTA only: q_full, kv_full[NKV], p_full, o_empty, unit_empty[2], drain
-  // both CTAs:     q_empty, kv_empty[NKV], s_full[NSBUF], pv_done[2], o_full, unit_full[2]
+  // both CTAs:     q_empty, kv_empty[NKV], s_full[NSBUF], o_full, unit_full[2]
   static constexpr int BAR_QFULL = 0;
   static constexpr int BAR_QEMPTY = 1;
   static constexpr int BAR_KVFULL = 2;
@@ -65,12 +65,11 @@ struct Fmha2Config {
   // of the other's, so one barrier per buffer keeps the 8 arrivals of a phase
   // from mixing tiles.
   static constexpr int BAR_PFULL = BAR_SFULL + NSBUF;  // [NSBUF]
-  // PV(t) retired, alternating between two barriers by tile parity. A rescale
-  // at tile t waits for PV(t-1) while only PV(t-3) is known to have retired:
-  // with one barrier the wanted phase could be two behind, where a parity wait
-  // cannot tell it from the one before. On barrier (t-1) % 2 it is at most one.
-  static constexpr int BAR_PVDONE = BAR_PFULL + NSBUF;  // [2]
-  static constexpr int BAR_OFULL = BAR_PVDONE + 2;
+  // "PV(t) retired" is kv_empty[t % NKV] (the commit that frees tile t's
+  // stage). A rescale at tile t waits for PV(t-1) while PV(t-3) is known to
+  // have retired, so the wanted phase of that stage barrier is at most one
+  // behind and its parity is unambiguous.
+  static constexpr int BAR_OFULL = BAR_PFULL + NSBUF;
   static constexpr int BAR_OEMPTY = BAR_OFULL + 1;
   static constexpr int BAR_UFULL = BAR_OEMPTY + 1;     // [2]
   static constexpr int BAR_UEMPTY = BAR_UFULL + 2;     // [2]
@@ -173,8 +172,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       ptx::mbar_init(bar(C::BAR_SFULL + b), 1);
       ptx::mbar_init(bar(C::BAR_PFULL + b), 2 * C::SOFTMAX_WARPS);  // both CTAs
     }
-    ptx::mbar_init(bar(C::BAR_PVDONE), 1);
-    ptx::mbar_init(bar(C::BAR_PVDONE + 1), 1);
     ptx::mbar_init(bar(C::BAR_OFULL), 1);
     ptx::mbar_init(bar(C::BAR_OEMPTY), 2 * C::SOFTMAX_WARPS);  // both CTAs
     for (int s = 0; s < 2; ++s) {
@@ -267,8 +264,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
     for (int s = 0; s < NKV; ++s)
       if (last_item[s] >= 0)
         bounded_wait(wc, bar(C::BAR_KVEMPTY + s), ((last_item[s] / NKV) & 1), false);
-  } else if (warp == C::MMA_WARP && lane == 0 && leader) {
+  } else if (warp == C::MMA_WARP && leader) {
     // =========================== 2-SM UMMA issuer ===========================
+    // The whole warp runs this loop in lockstep; elect.sync inside the
+    // tcgen05 wrappers picks the issuing lane.
     constexpr uint32_t IDESC_QK = ptx::make_idesc_f16(2 * BM, BN, BF16, false, false);
     constexpr uint32_t IDESC_PV = ptx::make_idesc_f16(2 * BM, D, BF16, false, true);
     const uint32_t q_s = sbase + C::OFF_Q, kv_s = sbase + C::OFF_KV;
@@ -283,7 +282,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       for (int kk = 0; kk < D / 16; ++kk) {
         const uint32_t offq = ((kk >> 2) * C::Q_CHUNK + (kk & 3) * 32) >> 4;
         const uint32_t offk = ((kk >> 2) * C::KH_CHUNK + (kk & 3) * 32) >> 4;
-        ptx::umma_ss_2sm(d_tmem, dq + offq, b0 + offk, IDESC_QK, kk > 0 ? 1u : 0u);
+        ptx::umma_ss_2sm_warp(d_tmem, dq + offq, b0 + offk, IDESC_QK, kk > 0 ? 1u : 0u);
       }
     };
     auto issue_pv = [&](uint32_t buf, int stage, bool first) {
@@ -292,25 +291,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       const uint64_t b0 = dv + ((stage * C::STAGE_BYTES) >> 4);
 #pragma unroll
       for (int kk = 0; kk < BN / 16; ++kk)  // P of keys 16kk.. at column 8kk (+32 past key 64)
-        ptx::umma_ts_2sm(d_tmem, p_tmem + kk * 8 + (kk >= 4 ? 32 : 0), b0 + ((kk * 2048) >> 4),
-                         IDESC_PV, (first && kk == 0) ? 0u : 1u);
+        ptx::umma_ts_2sm_warp(d_tmem, p_tmem + kk * 8 + (kk >= 4 ? 32 : 0),
+                              b0 + ((kk * 2048) >> 4), IDESC_PV, (first && kk == 0) ? 0u : 1u);
     };
-    Tracer tr(2);
+    Tracer trc(2);
+    auto tr = [&](int tag) { if (lane == 0) trc(tag); };
     uint32_t tcnt = 0;     // tiles issued = ring stage index = S/P buffer sequence
     uint32_t units = 0;
     bool ok = true;
-    auto stage_wait = [&](uint32_t t) {
-      return bounded_wait(wc, bar(C::BAR_KVFULL + t % NKV), (t / NKV) & 1);
+    // every lane waits; the warp proceeds only if all of them saw the phase
+    auto wait = [&](uint32_t b, uint32_t parity) {
+      return __all_sync(0xffffffffu, bounded_wait(wc, b, parity));
     };
+    auto stage_wait = [&](uint32_t t) { return wait(bar(C::BAR_KVFULL + t % NKV), (t / NKV) & 1); };
     for (int k = 0; ok; ++k) {
       const int slot = k & 1;
-      if (!bounded_wait_cl(wc, bar(C::BAR_UFULL + slot), (k >> 1) & 1)) break;
-      const int u = unit_ring[slot];
-      ptx::mbar_arrive(bar(C::BAR_UEMPTY + slot));
+      if (!__all_sync(0xffffffffu, bounded_wait_cl(wc, bar(C::BAR_UFULL + slot), (k >> 1) & 1)))
+        break;
+      const int u = __shfl_sync(0xffffffffu, unit_ring[slot], 0);
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar(C::BAR_UEMPTY + slot));
       if (u < 0) break;
       UnitInfo U;
       decode_unit<BM, BN>(u, args, U);
-      if (!bounded_wait(wc, bar(C::BAR_QFULL), k & 1)) break;
+      if (!wait(bar(C::BAR_QFULL), k & 1)) break;
       const int T = static_cast<int>(U.jhi - U.jlo);
       // S of up to NSBUF tiles ahead
       const int pre = T < C::NSBUF ? T : C::NSBUF;
@@ -319,32 +323,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
         if (!stage_wait(t)) { ok = false; break; }
         ptx::tc_fence_after();
         issue_s(t % C::NSBUF, t % NKV);
-        ptx::umma_commit_2sm(bar(C::BAR_SFULL + t % C::NSBUF), BOTH);
+        ptx::umma_commit_2sm_warp(bar(C::BAR_SFULL + t % C::NSBUF), BOTH);
         tr(20);
       }
       if (!ok) break;
-      if (T <= C::NSBUF) ptx::umma_commit_2sm(bar(C::BAR_QEMPTY), BOTH);
+      if (T <= C::NSBUF) ptx::umma_commit_2sm_warp(bar(C::BAR_QEMPTY), BOTH);
       for (int i = 0; i < T; ++i) {
         const uint32_t t = tcnt + i, b = t % C::NSBUF;
-        if (!bounded_wait(wc, bar(C::BAR_PFULL + b), (t / C::NSBUF) & 1)) { ok = false; break; }
+        if (!wait(bar(C::BAR_PFULL + b), (t / C::NSBUF) & 1)) { ok = false; break; }
         tr(21);
-        if (i == 0 && units > 0 && !bounded_wait(wc, bar(C::BAR_OEMPTY), (units - 1) & 1)) {
+        if (i == 0 && units > 0 && !wait(bar(C::BAR_OEMPTY), (units - 1) & 1)) {
           ok = false;
           break;
         }
         ptx::tc_fence_after();
         issue_pv(b, t % NKV, i == 0);
-        ptx::umma_commit_2sm(bar(C::BAR_KVEMPTY + t % NKV), BOTH);  // K and V halves of tile t
-        if (SOFTMAX) ptx::umma_commit_2sm(bar(C::BAR_PVDONE + (t & 1)), BOTH);
-        if (i == T - 1) ptx::umma_commit_2sm(bar(C::BAR_OFULL), BOTH);
+        // K and V halves of tile t are free, and O holds PV(t)
+        ptx::umma_commit_2sm_warp(bar(C::BAR_KVEMPTY + t % NKV), BOTH);
+        if (i == T - 1) ptx::umma_commit_2sm_warp(bar(C::BAR_OFULL), BOTH);
         tr(22);
         if (i + C::NSBUF < T) {  // S three tiles ahead, into the buffer P(t) just left
           const uint32_t t3 = t + C::NSBUF;
           if (!stage_wait(t3)) { ok = false; break; }
           ptx::tc_fence_after();
           issue_s(b, t3 % NKV);
-          ptx::umma_commit_2sm(bar(C::BAR_SFULL + b), BOTH);
-          if (i + C::NSBUF == T - 1) ptx::umma_commit_2sm(bar(C::BAR_QEMPTY), BOTH);
+          ptx::umma_commit_2sm_warp(bar(C::BAR_SFULL + b), BOTH);
+          if (i + C::NSBUF == T - 1) ptx::umma_commit_2sm_warp(bar(C::BAR_QEMPTY), BOTH);
           tr(20);
         }
       }
@@ -352,8 +356,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       tcnt += T;
       ++units;
     }
-    ptx::umma_commit_2sm(bar(C::BAR_DRAIN), 0x1);  // every 2-SM UMMA of this thread retired
+    ptx::umma_commit_2sm_warp(bar(C::BAR_DRAIN), 0x1);  // every 2-SM UMMA of this warp retired
     bounded_wait(wc, bar(C::BAR_DRAIN), 0, false);
+    __syncwarp();
   } else if (warp < C::SOFTMAX_WARPS) {
     // ======================= softmax / epilogue =======================
     const int quad = warp & 3, half = warp >> 2;
@@ -454,9 +459,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
               m_run = m_new;
             }
             if (!first_mine && __any_sync(0xffffffffu, need)) {
-              // O holds every earlier PV once PV(t-1) retired
+              // O holds every earlier PV once PV(t-1) retired (it frees that stage)
               const uint32_t prev = cnt - 1;
-              if (!bounded_wait(wc, bar(C::BAR_PVDONE + (prev & 1)), (prev >> 1) & 1)) {
+              if (!bounded_wait(wc, bar(C::BAR_KVEMPTY + prev % NKV), (prev / NKV) & 1)) {
                 ok = false;
                 break;
               }
