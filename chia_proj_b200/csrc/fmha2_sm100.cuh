@@ -116,6 +116,16 @@ __device__ __forceinline__ EpiConsts make_epi_consts(const KernelArgs &a, float 
   return kc;
 }
 
+// Key tiles of a unit are visited from the last to the first for ALiBi with a
+// positive slope: the bias slope * (j - i) then starts at its largest, the
+// running row maximum is set by the first tile, and later tiles never force
+// an O rescale (visited forwards, it would grow by slope * 128 per tile).
+// Every role of the kernel visits tiles in the same order.
+template <int KIND>
+__device__ __forceinline__ bool reverse_tiles(const KernelArgs &a, const UnitInfo &U) {
+  return KIND == KIND_ALIBI && a.head_param[U.h] > 0.f;
+}
+
 // Bounded wait on a local barrier that may receive arrivals from the other CTA.
 __device__ __forceinline__ bool bounded_wait_cl(const WaitCtx &c, uint32_t bar, uint32_t parity,
                                                 bool honour_abort = true) {
@@ -256,7 +266,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
                              static_cast<int>(U.m0) + BM * static_cast<int>(rank), U.r_res, U.h,
                              U.b);
       bool ok = true;
-      for (int64_t t = U.jlo; ok && t < U.jhi; ++t) ok = load_tile(t, U);
+      const bool rev = reverse_tiles<KIND>(args, U);
+      for (int64_t k2 = 0; ok && k2 < U.jhi - U.jlo; ++k2)
+        ok = load_tile(rev ? U.jhi - 1 - k2 : U.jlo + k2, U);
       if (!ok) break;
     }
     // Drain: this CTA's copies have landed once the even CTA released their
@@ -370,21 +382,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
     const uint32_t pfull0 = lbar(C::BAR_PFULL), oempty = lbar(C::BAR_OEMPTY);
     float *xch = reinterpret_cast<float *>(smem + C::OFF_XCH);
     uint32_t xcnt = 0;
-    // Hands v to the warp that owns the other column half of these rows and
-    // returns its value in `other`. Both warps call it in the same order; two
-    // slots keep a fast warp from overwriting a value the other has not read
-    // (it cannot reach exchange n+2 before the other arrived at n+1). The
-    // wait is bounded: false means the kernel is aborting.
-    auto exchange = [&](float v, float &other) -> bool {
-      const uint32_t slot = xcnt & 1, phase = (xcnt >> 1) & 1;
-      ++xcnt;
+    // Exchange of one float per row with the warp that owns the other column
+    // half of these rows: publish() hands v over without waiting, collect()
+    // returns the other warp's value of the same exchange. Both warps publish
+    // and collect in the same order. Two slots per quadrant keep a fast warp
+    // from overwriting a value the other has not read: a warp publishes
+    // exchange n+2 only after collecting n+1, which the other publishes only
+    // after collecting n. collect() waits with a bound: false means the
+    // kernel is aborting.
+    auto publish = [&](float v) {
+      const uint32_t slot = xcnt & 1;
       xch[slot * 256 + half * 128 + row] = v;
       __syncwarp();
-      const uint32_t xb = bar(C::BAR_XCH + quad * 2 + slot);
-      if (lane == 0) ptx::mbar_arrive(xb);
-      if (!bounded_wait(wc, xb, phase)) return false;
+      if (lane == 0) ptx::mbar_arrive(bar(C::BAR_XCH + quad * 2 + slot));
+    };
+    auto collect = [&](float &other) -> bool {
+      const uint32_t slot = xcnt & 1, phase = (xcnt >> 1) & 1;
+      ++xcnt;
+      if (!bounded_wait(wc, bar(C::BAR_XCH + quad * 2 + slot), phase)) return false;
       other = xch[slot * 256 + (half ^ 1) * 128 + row];
       return true;
+    };
+    auto exchange = [&](float v, float &other) -> bool {
+      publish(v);
+      return collect(other);
     };
     Tracer tr(warp == 0 ? 0 : 1);
     const bool tracing = warp == 0 && lane == 0;
@@ -412,7 +433,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       EpiConsts kc = make_epi_consts<KIND>(args, hp);
       float m_run = -INFINITY, l_run = 0.f;
       bool ok = true, first_mine = true;
-      for (int64_t t = U.jlo; t < U.jhi; ++t, ++cnt) {
+      const bool rev = reverse_tiles<KIND>(args, U);
+      for (int64_t k2 = 0; k2 < U.jhi - U.jlo; ++k2, ++cnt) {
+        const int64_t t = rev ? U.jhi - 1 - k2 : U.jlo + k2;
         const uint32_t buf = cnt % C::NSBUF;
         const uint32_t tS = tmem_base + lane_off + buf * 128 + half * 64;
         if (!bounded_wait(wc, bar(C::BAR_SFULL + buf), (cnt / C::NSBUF) & 1)) {
@@ -447,29 +470,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
               mx = softmax_pass1<KIND, 1>(sr, kc, rm);
             else
               mx = softmax_pass1<KIND, 2>(sr, kc, rm);
+            // The row maximum of the whole tile needs the other half's. After
+            // the first tile, P is computed optimistically against the running
+            // maximum, which stays exact unless the maximum grew by more than
+            // 2^8 (lazy rescale); the other half's value is collected only
+            // afterwards, when it has long been published.
+            publish(mx);
+            float lsum = 0.f;
+            if (!first_mine) lsum = softmax_pass2<BF16>(sr, m_run == -INFINITY ? 0.f : m_run, sink);
             float mx_other;
-            if (!exchange(mx, mx_other)) { ok = false; break; }
+            if (!collect(mx_other)) { ok = false; break; }
             mx = fmaxf(mx, mx_other);  // row maximum over the whole tile
             const float m_new = fmaxf(m_run, mx);
             const bool need = m_new > m_run + 8.0f;
-            float alpha = 1.0f;
-            if (need) {
-              alpha = ptx::ex2(m_run - m_new);
-              l_run *= alpha;
-              m_run = m_new;
-            }
-            if (!first_mine && __any_sync(0xffffffffu, need)) {
-              // O holds every earlier PV once PV(t-1) retired (it frees that stage)
-              const uint32_t prev = cnt - 1;
-              if (!bounded_wait(wc, bar(C::BAR_KVEMPTY + prev % NKV), (prev / NKV) & 1)) {
-                ok = false;
-                break;
+            if (first_mine || __any_sync(0xffffffffu, need)) {
+              float alpha = 1.0f;
+              if (need) {
+                alpha = ptx::ex2(m_run - m_new);
+                l_run *= alpha;
+                m_run = m_new;
               }
-              ptx::tc_fence_after();
-              rescale_rows<64>(tO, alpha);
+              if (!first_mine) {
+                ptx::tmem_wait_st();  // the optimistic P is written before it is replaced
+                // O holds every earlier PV once PV(t-1) retired (it frees that stage)
+                const uint32_t prev = cnt - 1;
+                if (!bounded_wait(wc, bar(C::BAR_KVEMPTY + prev % NKV), (prev / NKV) & 1)) {
+                  ok = false;
+                  break;
+                }
+                ptx::tc_fence_after();
+                rescale_rows<64>(tO, alpha);
+              }
+              // (re)compute P against the new maximum; P is not yet signalled
+              lsum = softmax_pass2<BF16>(sr, m_run == -INFINITY ? 0.f : m_run, sink);
             }
-            const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
-            l_run += softmax_pass2<BF16>(sr, m_use, sink);
+            l_run += lsum;
           } else {
             if (mode == 0)
               pointwise_tile<KIND, 0, BF16>(sr, kc, rm, sink);
