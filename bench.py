@@ -293,6 +293,8 @@ def run_ours(a):
     device = torch.device("cuda", local)
     if ws > 1:
         import datetime
+        # stdout carries exactly one JSON line: NCCL's own log goes to stderr
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=device)
     units = a.units
