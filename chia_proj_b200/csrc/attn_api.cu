@@ -326,8 +326,9 @@ int chia_attn_tile_plan(const chia_attn_params_t *p, int64_t row0, int32_t tile_
   int64_t lo, hi;
   chia::tile_range(g, row0, row0 + tile_m - 1, tile_n, lo, hi);
   uint64_t m = 0;
+  const chia::FullTiles ft = chia::full_tiles(g, row0, row0 + tile_m - 1, tile_n);
   for (int64_t t = lo; t < hi && t - lo < 64; ++t)
-    if (chia::tile_full(g, row0, row0 + tile_m - 1, tile_n, t)) m |= 1ull << (t - lo);
+    if (ft.full(t)) m |= 1ull << (t - lo);
   *tile_lo = lo;
   *tile_hi = hi;
   *full_mask = m;

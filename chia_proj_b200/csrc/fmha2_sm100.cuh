@@ -431,6 +431,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       const uint32_t span = band_empty ? 0u : static_cast<uint32_t>(bhi64 - blo64);
       const float hp = args.head_param != nullptr ? args.head_param[U.h] : 1.0f;
       EpiConsts kc = make_epi_consts<KIND>(args, hp);
+      const FullTiles ft = full_tiles(g, r0, r1, BN);
       float m_run = -INFINITY, l_run = 0.f;
       bool ok = true, first_mine = true;
       const bool rev = reverse_tiles<KIND>(args, U);
@@ -460,7 +461,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
           rm.i_rel = i - kv0;
           rm.dil = dil;
           kc.rel0 = static_cast<float>(kv0 - i);
-          const int mode = tile_full(g, r0, r1, BN, t) ? 0 : (dil == 1 ? 1 : 2);
+          const int mode = ft.full(t) ? 0 : (dil == 1 ? 1 : 2);
           const PSinkTmem sink{tS};  // P of these 64 keys -> first 32 of these columns
           if (SOFTMAX) {
             float mx;

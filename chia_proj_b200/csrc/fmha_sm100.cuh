@@ -774,6 +774,7 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
 
       const int i = static_cast<int>(U.m0) + w * BM + row;
       const int64_t r0 = U.m0 + w * BM, r1 = r0 + BM - 1;
+      const FullTiles ft = full_tiles(g, r0, r1, BN);
       int64_t blo64, bhi64;
       row_band(g, i, blo64, bhi64);
       const bool band_empty = bhi64 < blo64;
@@ -824,7 +825,7 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
         rm.i_rel = i - kv0;
         rm.dil = dil;
         kc.rel0 = static_cast<float>(kv0 - i);  // (j - i) of column 0, exact in fp32
-        const int mode = tile_full(g, r0, r1, BN, t) ? 0 : (dil == 1 ? 1 : 2);
+        const int mode = ft.full(t) ? 0 : (dil == 1 ? 1 : 2);
         if (SOFTMAX) {
           float mx;
           if (mode == 0)

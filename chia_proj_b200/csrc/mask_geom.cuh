@@ -82,6 +82,36 @@ CHIA_HD bool tile_full(const MaskGeom &g, int64_t r0, int64_t r1, int tn, int64_
   return lo_last <= c0 && hi_first >= c1;
 }
 
+// tile_full() for every key tile of one query tile [r0, r1], computed once:
+// the comparisons of tile_full() turned into tile-index bounds. Because lo()
+// and hi() are non-decreasing, the fully visible tiles are the prefix tiles
+// plus one contiguous band range, all within the tiles that end inside S_kv.
+struct FullTiles {
+  int32_t kv_end;   // tiles t < kv_end end inside S_kv
+  int32_t pre_end;  // tiles t < pre_end lie inside the prefix
+  int32_t band_lo, band_hi;  // band tiles [band_lo, band_hi) (dilation 1 only)
+  CHIA_HD bool full(int64_t t) const {
+    return t < kv_end && (t < pre_end || (t >= band_lo && t < band_hi));
+  }
+};
+
+CHIA_HD FullTiles full_tiles(const MaskGeom &g, int64_t r0, int64_t r1, int tn) {
+  if (r1 > g.sq - 1) r1 = g.sq - 1;
+  FullTiles f;
+  f.kv_end = static_cast<int32_t>(g.skv / tn);     // (t + 1) tn <= skv
+  f.pre_end = static_cast<int32_t>(g.prefix / tn);  // (t + 1) tn <= prefix
+  f.band_lo = f.band_hi = 0;
+  if (g.dil == 1) {
+    int64_t lo_last, hi_last, lo_first, hi_first;
+    row_band(g, r1, lo_last, hi_last);
+    row_band(g, r0, lo_first, hi_first);
+    // lo(r1) <= t tn  and  t tn + tn - 1 <= hi(r0)
+    f.band_lo = static_cast<int32_t>((imax64(lo_last, 0) + tn - 1) / tn);
+    f.band_hi = static_cast<int32_t>(imax64(hi_first + 1, 0) / tn);
+  }
+  return f;
+}
+
 // Element visibility with the row band already known.
 CHIA_HD bool visible(const MaskGeom &g, int64_t i, int64_t j, int64_t lo, int64_t hi) {
   if (j < g.prefix) return true;

@@ -89,9 +89,14 @@ def test_tile_plan_covers_and_full_tiles_are_full(lib, mask):
             if cols_needed.numel():
                 assert lo * BN <= int(cols_needed.min()) and int(cols_needed.max()) < hi * BN
             for t in range(lo, hi):
+                blk = rows[:, t * BN:(t + 1) * BN]
+                complete = blk.shape[1] == BN and bool(blk.all())
                 if bits >> (t - lo) & 1:
-                    blk = rows[:, t * BN:(t + 1) * BN]
-                    assert blk.shape[1] == BN and bool(blk.all()), (mask, S, row0, t)
+                    assert complete, (mask, S, row0, t)
+                elif mask.dilation == 1 and mask.prefix == 0 and t - lo < 64:
+                    # without a prefix a completely visible tile lies in every
+                    # row's band, which the plan must recognise
+                    assert not complete, ("missed full tile", mask, S, row0, t)
 
 
 def test_reference_masks_skip_work(lib):
