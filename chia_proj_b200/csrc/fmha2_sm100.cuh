@@ -144,7 +144,10 @@ __device__ __forceinline__ bool bounded_wait_cl(const WaitCtx &c, uint32_t bar, 
   }
 }
 
-template <int D, bool BF16, int KIND>
+// MASKED = false: every key tile of every unit is fully visible (the host
+// checks: no window, block or dilation and S_kv a multiple of 128), so the
+// element-wise mask code is left out of the kernel.
+template <int D, bool BF16, int KIND, bool MASKED>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THREADS, 1)
     fmha2_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_kh,
@@ -461,7 +464,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
           rm.i_rel = i - kv0;
           rm.dil = dil;
           kc.rel0 = static_cast<float>(kv0 - i);
-          const int mode = ft.full(t) ? 0 : (dil == 1 ? 1 : 2);
+          const int mode = (!MASKED || ft.full(t)) ? 0 : (dil == 1 ? 1 : 2);
           const PSinkTmem sink{tS};  // P of these 64 keys -> first 32 of these columns
           if (SOFTMAX) {
             float mx;

@@ -282,3 +282,15 @@ def test_running_max_rises_every_tile(cuda, op, D, kw):
     check(out, oracle.run_op(op, q, k, v, **kw), op)
     for _ in range(3):
         assert torch.equal(out, run(op, q, k, v, **kw))
+
+
+@pytest.mark.parametrize("S", [1024, 1000])
+@pytest.mark.parametrize("op,kw", [("softcap_gemma2", dict(cap=50.0, causal=False)),
+                                   ("sigmoid_attn", dict(causal=False, bias=-2.0)),
+                                   ("relu_attn", dict(causal=False, out_scale=1e-3))])
+def test_non_causal_with_and_without_mask_code(cuda, op, kw, S):
+    """Non-causal masks with S a multiple of 128 run the kernel built without
+    element-wise mask code; S = 1000 leaves a ragged last key tile that must
+    still be masked. Both against the oracle."""
+    q, k, v = gen(2, 2, S, 128, torch.bfloat16, seed=41)
+    check(run(op, q, k, v, **kw), oracle.run_op(op, q, k, v, **kw), f"{op} S={S}")
