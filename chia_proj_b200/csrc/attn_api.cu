@@ -183,7 +183,8 @@ int launch_one(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &
 // head_dim 128: CTA pairs with 2-SM UMMAs (fmha2_sm100.cuh)
 template <bool BF16, int KIND, bool MASKED>
 int launch_pair(const CUtensorMap &mq, const CUtensorMap &mkh, const CUtensorMap &mvh,
-                const chia::KernelArgs &a, int64_t nunits, cudaStream_t stream) {
+                const CUtensorMap &mo, const chia::KernelArgs &a, int64_t nunits,
+                cudaStream_t stream) {
   using Cfg = chia::Fmha2Config<128>;
   auto kern = chia::fmha2_fwd_kernel<128, BF16, KIND, MASKED>;
   static std::atomic<uint32_t> configured{0};
@@ -208,24 +209,25 @@ int launch_pair(const CUtensorMap &mq, const CUtensorMap &mkh, const CUtensorMap
   const int64_t pairs_max = max_pairs[dev & 31].load(std::memory_order_relaxed);
   const int64_t pairs = nunits < pairs_max ? nunits : pairs_max;
   kern<<<static_cast<unsigned>(2 * pairs), Cfg::THREADS, Cfg::SMEM_ALLOC, stream>>>(mq, mkh, mvh,
-                                                                                   a);
+                                                                                   mo, a);
   return cudaGetLastError() == cudaSuccess ? CHIA_OK : CHIA_ERR_LAUNCH;
 }
 
 template <bool BF16, bool MASKED>
 int launch_pair_kind(int kind, const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
-                     const chia::KernelArgs &a, int64_t nunits, cudaStream_t s) {
+                     const CUtensorMap &mo, const chia::KernelArgs &a, int64_t nunits,
+                     cudaStream_t s) {
   switch (kind) {
     case chia::KIND_SOFTMAX:
-      return launch_pair<BF16, chia::KIND_SOFTMAX, MASKED>(mq, mk, mv, a, nunits, s);
+      return launch_pair<BF16, chia::KIND_SOFTMAX, MASKED>(mq, mk, mv, mo, a, nunits, s);
     case chia::KIND_SOFTCAP:
-      return launch_pair<BF16, chia::KIND_SOFTCAP, MASKED>(mq, mk, mv, a, nunits, s);
+      return launch_pair<BF16, chia::KIND_SOFTCAP, MASKED>(mq, mk, mv, mo, a, nunits, s);
     case chia::KIND_ALIBI:
-      return launch_pair<BF16, chia::KIND_ALIBI, MASKED>(mq, mk, mv, a, nunits, s);
+      return launch_pair<BF16, chia::KIND_ALIBI, MASKED>(mq, mk, mv, mo, a, nunits, s);
     case chia::KIND_SIGMOID:
-      return launch_pair<BF16, chia::KIND_SIGMOID, MASKED>(mq, mk, mv, a, nunits, s);
+      return launch_pair<BF16, chia::KIND_SIGMOID, MASKED>(mq, mk, mv, mo, a, nunits, s);
     case chia::KIND_RELU:
-      return launch_pair<BF16, chia::KIND_RELU, MASKED>(mq, mk, mv, a, nunits, s);
+      return launch_pair<BF16, chia::KIND_RELU, MASKED>(mq, mk, mv, mo, a, nunits, s);
   }
   return CHIA_ERR_INVALID_ARGUMENT;
 }
@@ -395,17 +397,20 @@ int chia_attn_fwd(const chia_attn_params_t *p, void *stream) {
   if (D == 128) {
     // K in half tiles of 64 keys (one per CTA of the pair); V as loaded above
     // (box of 128 keys x 64 columns; each CTA takes one column chunk)
-    CUtensorMap mkh;
+    CUtensorMap mkh, mo;
     if (!encode_map(&mkh, p->k, p->dtype, D, g.skv, dv.vdil, p->heads, p->batch, p->k_stride, 64))
+      return CHIA_ERR_LAUNCH;
+    // output through TMA stores, in the same 5-D view as Q
+    if (!encode_map(&mo, p->o, p->dtype, D, g.sq, dv.vdil, p->heads, p->batch, p->o_stride))
       return CHIA_ERR_LAUNCH;
     // every tile of every unit fully visible: the kernel without mask code
     const bool all_full = g.left < 0 && g.right < 0 && g.block == 0 && g.dil == 1 &&
                           g.skv % 128 == 0;
     if (all_full)
-      return bf16 ? launch_pair_kind<true, false>(kind, mq, mkh, mv, a, nunits, s)
-                  : launch_pair_kind<false, false>(kind, mq, mkh, mv, a, nunits, s);
-    return bf16 ? launch_pair_kind<true, true>(kind, mq, mkh, mv, a, nunits, s)
-                : launch_pair_kind<false, true>(kind, mq, mkh, mv, a, nunits, s);
+      return bf16 ? launch_pair_kind<true, false>(kind, mq, mkh, mv, mo, a, nunits, s)
+                  : launch_pair_kind<false, false>(kind, mq, mkh, mv, mo, a, nunits, s);
+    return bf16 ? launch_pair_kind<true, true>(kind, mq, mkh, mv, mo, a, nunits, s)
+                : launch_pair_kind<false, true>(kind, mq, mkh, mv, mo, a, nunits, s);
   }
   return bf16 ? launch_kind<64, true>(kind, mq, mk, mv, a, nblocks, s)
               : launch_kind<64, false>(kind, mq, mk, mv, a, nblocks, s);

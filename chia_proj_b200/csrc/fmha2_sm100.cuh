@@ -21,6 +21,11 @@
 //   per tile i:  once P(t_i) is ready, O += P(t_i) V(t_i), then S(t_{i+3})
 // into the buffer P(t_i) just left (UMMAs of one thread run in order).
 // K and V halves of a tile share one ring stage (one wait, one release).
+// Q is double-buffered by unit, so the next unit's Q arrives while the
+// current one runs. Once a unit's MMAs have retired, its Q buffer stages
+// the unit's output: the softmax warps write O (16-bit, 128-byte swizzle)
+// there, and the load thread stores it with TMA before it loads the Q of
+// the unit two ahead into the same buffer.
 //
 // Warps per CTA: 0-7 two softmax warpgroups; warp w owns TMEM lanes (query
 // rows) 32 (w % 4) .. +31 and key columns 64 (w / 4) .. +63 of every tile, so
@@ -50,15 +55,15 @@ struct Fmha2Config {
   static constexpr int STAGE_BYTES = 2 * HALF_BYTES;  // [K half | V half] of one tile
   static constexpr int NKV = 5;                       // ring stages (160 KB)
   static constexpr int NSBUF = 3;                     // S/P buffers in TMEM
-  static constexpr int OFF_Q = 0;
-  static constexpr int OFF_KV = OFF_Q + Q_BYTES;
+  static constexpr int OFF_Q = 0;                  // two Q buffers, alternating by unit
+  static constexpr int OFF_KV = OFF_Q + 2 * Q_BYTES;
   static constexpr int OFF_BAR = OFF_KV + NKV * STAGE_BYTES;
   // barriers (same offsets in both CTAs)
-  // even CTA only: q_full, kv_full[NKV], p_full, o_empty, unit_empty[2], drain
-  // both CTAs:     q_empty, kv_empty[NKV], s_full[NSBUF], o_full, unit_full[2]
-  static constexpr int BAR_QFULL = 0;
-  static constexpr int BAR_QEMPTY = 1;
-  static constexpr int BAR_KVFULL = 2;
+  // even CTA only: q_full[2], kv_full[NKV], p_full, o_empty, unit_empty[2], drain
+  // both CTAs:     o_staged[2], kv_empty[NKV], s_full[NSBUF], o_full, unit_full[2]
+  static constexpr int BAR_QFULL = 0;     // [2] Q of the unit using buffer b landed
+  static constexpr int BAR_OSTAGED = 2;   // [2] O of the unit using buffer b is in it
+  static constexpr int BAR_KVFULL = 4;
   static constexpr int BAR_KVEMPTY = BAR_KVFULL + NKV;
   static constexpr int BAR_SFULL = BAR_KVEMPTY + NKV;  // [NSBUF]
   // P ready, per S/P buffer: one CTA's softmax may run up to two tiles ahead
@@ -82,7 +87,10 @@ struct Fmha2Config {
   // float [2 parity][2 column half][128 rows]
   static constexpr int OFF_XCH = OFF_MISC + 16;
   static constexpr int SMEM_BYTES = OFF_XCH + 2 * 2 * 128 * 4;
-  static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;
+  // No slack for aligning the base: the dynamic shared memory of a kernel
+  // without static shared memory starts 1024-byte aligned (checked at run
+  // time), and the second Q buffer needs the room.
+  static constexpr int SMEM_ALLOC = SMEM_BYTES;
   static constexpr int THREADS = 320;
   static constexpr int SOFTMAX_WARPS = 8;
   static constexpr int MMA_WARP = 8;
@@ -151,15 +159,21 @@ template <int D, bool BF16, int KIND, bool MASKED>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THREADS, 1)
     fmha2_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_kh,
-                     const __grid_constant__ CUtensorMap tm_vh, const KernelArgs args) {
+                     const __grid_constant__ CUtensorMap tm_vh,
+                     const __grid_constant__ CUtensorMap tm_o, const KernelArgs args) {
   using C = Fmha2Config<D>;
   constexpr int BM = C::BM, BN = C::BN, NKV = C::NKV;
   constexpr bool SOFTMAX = (KIND == KIND_SOFTMAX || KIND == KIND_SOFTCAP || KIND == KIND_ALIBI);
 
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t sbase = ptx::smem_u32(smem);
+  // The 128-byte-swizzled tiles need a 1024-byte aligned base. Both CTAs of a
+  // pair share the layout, so both leave here together, before any cluster
+  // barrier; the status word reports it.
+  if (sbase & 1023u) {
+    if (threadIdx.x == 0 && args.status) atomicOr(args.status, 4 /* CHIA_ERR_LAUNCH */);
+    return;
+  }
   auto bar = [&](int idx) -> uint32_t { return sbase + C::OFF_BAR + idx * 8; };
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::OFF_MISC);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::OFF_MISC + 4);
@@ -175,8 +189,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
   auto lbar = [&](int idx) -> uint32_t { return ptx::mapa(bar(idx), 0); };
 
   if (threadIdx.x == 0) {
-    ptx::mbar_init(bar(C::BAR_QFULL), 2);
-    ptx::mbar_init(bar(C::BAR_QEMPTY), 1);
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(bar(C::BAR_QFULL + b), 2);                   // both CTAs' Q loads
+      ptx::mbar_init(bar(C::BAR_OSTAGED + b), C::SOFTMAX_WARPS);  // this CTA's softmax warps
+    }
     for (int s = 0; s < NKV; ++s) {
       ptx::mbar_init(bar(C::BAR_KVFULL + s), 2);
       ptx::mbar_init(bar(C::BAR_KVEMPTY + s), 1);
@@ -201,6 +217,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
     ptx::tma_prefetch_desc(&tm_q);
     ptx::tma_prefetch_desc(&tm_kh);
     ptx::tma_prefetch_desc(&tm_vh);
+    ptx::tma_prefetch_desc(&tm_o);
   }
   if (warp == C::MMA_WARP) {
     ptx::tmem_alloc_2sm(ptx::smem_u32(tmem_slot), C::TMEM_COLS);
@@ -238,7 +255,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       ++n;
       return true;
     };
+    // O of the unit that used Q buffer b (this CTA's k_unit-th unit): once
+    // this CTA's softmax warps have staged it there, store this CTA's 128
+    // rows with TMA (rows past the sequence end are not written) and wait
+    // until the store has read the buffer.
+    UnitInfo uq[2];
+    auto store_o = [&](int b, int k_unit) -> bool {
+      if (!bounded_wait(wc, bar(C::BAR_OSTAGED + b), (k_unit >> 1) & 1)) return false;
+      const UnitInfo &V = uq[b];
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c)
+        ptx::tma_store_5d(&tm_o, sbase + C::OFF_Q + b * C::Q_BYTES + c * C::Q_CHUNK, c * 64,
+                          static_cast<int>(V.m0) + BM * static_cast<int>(rank), V.r_res, V.h, V.b);
+      ptx::bulk_commit_group();
+      ptx::bulk_wait_read_all();
+      return true;
+    };
+    int k_end = 0;  // units taken
+    bool clean = false;
     for (int k = 0;; ++k) {
+      k_end = k;
       const int slot = k & 1;
       int u;
       if (leader) {
@@ -256,24 +292,35 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
         u = unit_ring[slot];
         ptx::mbar_arrive_cluster(lbar(C::BAR_UEMPTY + slot));
       }
-      if (u < 0) break;
+      if (u < 0) {
+        clean = true;
+        break;
+      }
       UnitInfo U;
       decode_unit<BM, BN>(u, args, U);
+      // Q buffer qb held unit k-2, whose output is staged there: store it first
+      const int qb = k & 1;
+      if (k >= 2 && !store_o(qb, k - 2)) break;
+      uq[qb] = U;
       // this CTA's query tile (zero-filled by TMA when past the sequence end)
-      if (k > 0 && !bounded_wait(wc, bar(C::BAR_QEMPTY), (k - 1) & 1)) break;
-      const uint32_t qfull = lbar(C::BAR_QFULL);
+      const uint32_t qfull = lbar(C::BAR_QFULL + qb);
       ptx::mbar_arrive_expect_tx_remote(qfull, C::Q_BYTES);
 #pragma unroll
       for (int c = 0; c < D / 64; ++c)
-        ptx::tma_load_5d_2sm(sbase + C::OFF_Q + c * C::Q_CHUNK, &tm_q, qfull, c * 64,
-                             static_cast<int>(U.m0) + BM * static_cast<int>(rank), U.r_res, U.h,
-                             U.b);
+        ptx::tma_load_5d_2sm(sbase + C::OFF_Q + qb * C::Q_BYTES + c * C::Q_CHUNK, &tm_q, qfull,
+                             c * 64, static_cast<int>(U.m0) + BM * static_cast<int>(rank), U.r_res,
+                             U.h, U.b);
       bool ok = true;
       const bool rev = reverse_tiles<KIND>(args, U);
       for (int64_t k2 = 0; ok && k2 < U.jhi - U.jlo; ++k2)
         ok = load_tile(rev ? U.jhi - 1 - k2 : U.jlo + k2, U);
       if (!ok) break;
     }
+    // outputs of the last two units
+    if (clean)
+      for (int j = k_end >= 2 ? k_end - 2 : 0; j < k_end; ++j)
+        if (!store_o(j & 1, j)) break;
+    ptx::bulk_wait_all();
     // Drain: this CTA's copies have landed once the even CTA released their
     // slots; on an abort the bounded waits below outlast any copy in flight.
     for (int s = 0; s < NKV; ++s)
@@ -286,7 +333,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
     constexpr uint32_t IDESC_QK = ptx::make_idesc_f16(2 * BM, BN, BF16, false, false);
     constexpr uint32_t IDESC_PV = ptx::make_idesc_f16(2 * BM, D, BF16, false, true);
     const uint32_t q_s = sbase + C::OFF_Q, kv_s = sbase + C::OFF_KV;
-    const uint64_t dq = ptx::make_sdesc_sw128(q_s, 16, 1024);
+    const uint64_t dq0 = ptx::make_sdesc_sw128(q_s, 16, 1024);
+    uint64_t dq = dq0;  // Q buffer of the current unit
     const uint64_t dk = ptx::make_sdesc_sw128(kv_s, 16, 1024);
     const uint64_t dv = ptx::make_sdesc_sw128(kv_s + C::HALF_BYTES, C::HALF_BYTES, 1024);
     constexpr uint16_t BOTH = 0x3;
@@ -329,7 +377,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       if (u < 0) break;
       UnitInfo U;
       decode_unit<BM, BN>(u, args, U);
-      if (!wait(bar(C::BAR_QFULL), k & 1)) break;
+      if (!wait(bar(C::BAR_QFULL + (k & 1)), (k >> 1) & 1)) break;
+      dq = dq0 + (((k & 1) * C::Q_BYTES) >> 4);
       const int T = static_cast<int>(U.jhi - U.jlo);
       // S of up to NSBUF tiles ahead
       const int pre = T < C::NSBUF ? T : C::NSBUF;
@@ -342,7 +391,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
         tr(20);
       }
       if (!ok) break;
-      if (T <= C::NSBUF) ptx::umma_commit_2sm_warp(bar(C::BAR_QEMPTY), BOTH);
       for (int i = 0; i < T; ++i) {
         const uint32_t t = tcnt + i, b = t % C::NSBUF;
         if (!wait(bar(C::BAR_PFULL + b), (t / C::NSBUF) & 1)) { ok = false; break; }
@@ -363,7 +411,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
           ptx::tc_fence_after();
           issue_s(b, t3 % NKV);
           ptx::umma_commit_2sm_warp(bar(C::BAR_SFULL + b), BOTH);
-          if (i + C::NSBUF == T - 1) ptx::umma_commit_2sm_warp(bar(C::BAR_QEMPTY), BOTH);
           tr(20);
         }
       }
@@ -553,17 +600,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       }
       if (!bounded_wait(wc, bar(C::BAR_OFULL), units & 1)) break;
       ptx::tc_fence_after();
-      const bool row_ok = U.wg_on(w) && i < g.sq;
-      const int64_t real_row = static_cast<int64_t>(i) * args.vdil + U.r_res;
-      uint8_t *orow = reinterpret_cast<uint8_t *>(args.o) +
-                      2 * (U.b * args.o_sb + static_cast<int64_t>(U.h) * args.o_sh +
-                           real_row * args.o_ss + half * 64);
       trs(14);
-      store_rows<64, BF16>(tO, inv, row_ok, orow);
-      trs(15);
+      uint32_t o[2][32];
+      ptx::tmem_ld32(tO, o[0]);
+      ptx::tmem_ld32(tO + 32, o[1]);
+      ptx::tmem_wait_ld();
+      ptx::reg_fence(o[0]);
+      ptx::reg_fence(o[1]);
+      // O is in registers: the MMA may start the next unit's PV
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive_remote(oempty);
+      // stage this row's 64 columns (16-bit) in the unit's Q buffer, column
+      // chunk `half`, in the 128-byte swizzle of the output tensor map
+      uint32_t pk[32];
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          pk[c * 16 + e] = pack2<BF16>(__uint_as_float(o[c][2 * e]) * inv,
+                                       __uint_as_float(o[c][2 * e + 1]) * inv);
+      const uint32_t qbuf = sbase + C::OFF_Q + (units & 1) * C::Q_BYTES + half * C::Q_CHUNK;
+      store_p_chunk(qbuf + row * 128, 0, row & 7, pk);
+      ptx::fence_proxy_async_smem();  // visible to the TMA store
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar(C::BAR_OSTAGED + (units & 1)));
+      trs(15);
       ++units;
     }
   }

@@ -89,6 +89,28 @@ __device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap *map
       : "memory");
 }
 
+// TMA tensor store of a box from this CTA's shared memory (bulk async-group
+// of the issuing thread); out-of-range parts of the box are not written.
+__device__ __forceinline__ void tma_store_5d(const CUtensorMap *map, uint32_t src, int c0, int c1,
+                                             int c2, int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5, %6}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// The thread's committed bulk stores have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read_all() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// The thread's committed bulk stores are complete.
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 // ------------------------------------------------------------------ tcgen05
 // Allocate `ncols` TMEM columns (power of two >= 32); the base address is
 // written to shared memory at `dst_smem`. Executed by one whole warp.
