@@ -52,7 +52,7 @@ class AttnParams(ctypes.Structure):
         ("head_dim", ctypes.c_int32),
         ("norm", ctypes.c_int32),
         ("mod", ctypes.c_int32),
-        ("reserved0", ctypes.c_int32),
+        ("heads_kv", ctypes.c_int32),
         ("batch", ctypes.c_int64),
         ("heads", ctypes.c_int64),
         ("seqlen_q", ctypes.c_int64),

@@ -87,6 +87,8 @@ int validate(const chia_attn_params_t *p) {
   if (p->norm != CHIA_NORM_SOFTMAX && p->mod != CHIA_MOD_NONE) return CHIA_ERR_UNSUPPORTED;
   if (p->batch < 1 || p->heads < 1 || p->seqlen_q < 1 || p->seqlen_kv < 1)
     return CHIA_ERR_INVALID_ARGUMENT;
+  if (p->heads_kv < 0 || (p->heads_kv > 0 && p->heads % p->heads_kv != 0))
+    return CHIA_ERR_INVALID_ARGUMENT;
   // With S_q <= S_kv the diagonal key j = i is visible for every row under
   // every mask this ABI can describe, so no query row is left without keys.
   if (p->seqlen_q > p->seqlen_kv) return CHIA_ERR_UNSUPPORTED;
@@ -356,14 +358,16 @@ int chia_attn_fwd(const chia_attn_params_t *p, void *stream) {
   const MaskGeom &g = dv.geom;
   const int D = p->head_dim;
   CUtensorMap mq, mk, mv;
+  const int64_t hkv = p->heads_kv > 0 ? p->heads_kv : p->heads;  // K/V heads
   if (!encode_map(&mq, p->q, p->dtype, D, g.sq, dv.vdil, p->heads, p->batch, p->q_stride) ||
-      !encode_map(&mk, p->k, p->dtype, D, g.skv, dv.vdil, p->heads, p->batch, p->k_stride) ||
-      !encode_map(&mv, p->v, p->dtype, D, g.skv, dv.vdil, p->heads, p->batch, p->v_stride))
+      !encode_map(&mk, p->k, p->dtype, D, g.skv, dv.vdil, hkv, p->batch, p->k_stride) ||
+      !encode_map(&mv, p->v, p->dtype, D, g.skv, dv.vdil, hkv, p->batch, p->v_stride))
     return CHIA_ERR_LAUNCH;
 
   chia::KernelArgs a{};
   a.mask = g;
   a.heads = static_cast<int32_t>(p->heads);
+  a.group = static_cast<int32_t>(p->heads / hkv);
   a.vdil = dv.vdil;
   const int64_t rows_per_unit = 2 * 128;
   const int64_t nqb = (g.sq + rows_per_unit - 1) / rows_per_unit;
@@ -398,7 +402,7 @@ int chia_attn_fwd(const chia_attn_params_t *p, void *stream) {
     // K in half tiles of 64 keys (one per CTA of the pair); V as loaded above
     // (box of 128 keys x 64 columns; each CTA takes one column chunk)
     CUtensorMap mkh, mo;
-    if (!encode_map(&mkh, p->k, p->dtype, D, g.skv, dv.vdil, p->heads, p->batch, p->k_stride, 64))
+    if (!encode_map(&mkh, p->k, p->dtype, D, g.skv, dv.vdil, hkv, p->batch, p->k_stride, 64))
       return CHIA_ERR_LAUNCH;
     // output through TMA stores, in the same 5-D view as Q
     if (!encode_map(&mo, p->o, p->dtype, D, g.sq, dv.vdil, p->heads, p->batch, p->o_stride))

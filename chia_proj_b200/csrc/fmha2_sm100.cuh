@@ -247,9 +247,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       for (int c = 0; c < D / 64; ++c)
         ptx::tma_load_5d_2sm(dst + c * C::KH_CHUNK, &tm_kh, full, c * 64,
                              static_cast<int>(t * BN) + C::KH_ROWS * static_cast<int>(rank),
-                             U.r_res, U.h, U.b);
+                             U.r_res, U.h / args.group, U.b);
       ptx::tma_load_5d_2sm(dst + C::HALF_BYTES, &tm_vh, full, 64 * static_cast<int>(rank),
-                           static_cast<int>(t * BN), U.r_res, U.h, U.b);
+                           static_cast<int>(t * BN), U.r_res, U.h / args.group, U.b);
       tr(30);
       last_item[s] = n;
       ++n;

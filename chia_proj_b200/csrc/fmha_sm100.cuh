@@ -54,6 +54,7 @@ enum Kind : int {
 struct KernelArgs {
   MaskGeom mask;        // geometry in (virtual) row / key index space
   int32_t heads;        // H
+  int32_t group;        // q heads per K/V head (grouped-query attention; 1 = none)
   int32_t vdil;         // rows of one virtual head are i' * vdil + r (1 = plain)
   int32_t n_qblocks;    // ceil(sq / (NQ * BM))
   int32_t n_vheads;     // B * H * vdil
@@ -540,7 +541,7 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
         for (int c = 0; c < C::NCHUNK; ++c)
           ptx::tma_load_5d(sbase + C::OFF_KV + s * C::KV_TILE_BYTES + c * C::CHUNK_KV_BYTES, map,
                            bar(C::BAR_KVFULL + s), c * 64, static_cast<int>(j * BN), U.r_res,
-                           U.h, U.b);
+                           U.h / args.group, U.b);
         last_item[s] = n;
         ++n;
         return true;

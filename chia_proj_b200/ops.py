@@ -160,7 +160,9 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     """Generic forward attention: ``norm(mask(mod(q.k * scale))) @ v``.
 
     ``q, k, v``: CUDA tensors ``[B, H, S, D]`` (bf16 / fp16; fp32 computed as
-    bf16), ``D`` in {64, 128}. ``head_param``: ALiBi slopes (``mod="alibi"``)
+    bf16), ``D`` in {64, 128}. ``k`` and ``v`` may have ``H_kv`` heads with
+    ``H % H_kv == 0`` (grouped-query attention: query head ``h`` reads K/V
+    head ``h // (H // H_kv)``). ``head_param``: ALiBi slopes (``mod="alibi"``)
     or logit multipliers (``mod="temp"``), one per head. ``schedule``:
     ``"dynamic"`` balances work units over the SMs with a per-device
     workspace; ``"static"`` assigns them round-robin and uses no workspace.
@@ -180,7 +182,9 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     if not (q.device == k.device == v.device):
         raise ValueError("q, k, v must be on one device")
     B, H, S, D = q.shape
-    if k.shape != (B, H, k.shape[2], D) or v.shape != k.shape:
+    Hkv = k.shape[1]
+    if (k.shape != (B, Hkv, k.shape[2], D) or v.shape != k.shape or Hkv < 1
+            or H % Hkv != 0):
         raise ValueError(f"shape mismatch q{tuple(q.shape)} k{tuple(k.shape)} v{tuple(v.shape)}")
     if D not in (64, 128):
         raise ValueError(f"head_dim {D} unsupported (64 or 128)")
@@ -213,6 +217,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     p.norm = _NORMS[norm]
     p.mod = _MODS[mod]
     p.batch, p.heads, p.seqlen_q, p.seqlen_kv = B, H, S, k.shape[2]
+    p.heads_kv = Hkv
     p.q, p.k, p.v, p.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr()
     for field, t in (("q_stride", q), ("k_stride", k), ("v_stride", v), ("o_stride", o)):
         getattr(p, field)[:] = t.stride()[:3]

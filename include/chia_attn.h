@@ -96,7 +96,10 @@ typedef struct chia_attn_params {
   int32_t head_dim;    /* D: 64 or 128                                      */
   int32_t norm;        /* enum chia_norm                                    */
   int32_t mod;         /* enum chia_mod                                     */
-  int32_t reserved0;
+  int32_t heads_kv;    /* K/V heads (grouped-query attention): q head h
+                          reads K/V head h / (heads / heads_kv); must divide
+                          heads; 0 = heads. No counterpart in the reference,
+                          whose operators take K/V with all H heads.        */
 
   int64_t batch;     /* B                                                  */
   int64_t heads;     /* H                                                  */

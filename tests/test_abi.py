@@ -95,6 +95,8 @@ def _valid_params():
     (lambda p: setattr(p, "mod", N.MOD_ALIBI), 1),   # ALiBi without slopes
     (lambda p: (setattr(p, "mod", N.MOD_SOFTCAP), setattr(p, "softcap", 0.0)), 1),
     (lambda p: setattr(p, "scale", float("nan")), 1),
+    (lambda p: setattr(p, "heads_kv", 3), 1),    # 4 query heads, 3 K/V heads
+    (lambda p: setattr(p, "heads_kv", -1), 1),
 ])
 def test_argument_errors_are_reported_before_launch(lib, mutate, code):
     p = _valid_params()

@@ -294,3 +294,21 @@ def test_non_causal_with_and_without_mask_code(cuda, op, kw, S):
     still be masked. Both against the oracle."""
     q, k, v = gen(2, 2, S, 128, torch.bfloat16, seed=41)
     check(run(op, q, k, v, **kw), oracle.run_op(op, q, k, v, **kw), f"{op} S={S}")
+
+
+# ------------------------------------------------------ grouped-query K/V
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("op,kw", [("softcap_gemma2", {}), ("bias_sliding_window", {}),
+                                   ("bias_alibi", {}), ("sigmoid_attn", {}),
+                                   ("relu_attn", dict(causal=False, out_scale=1e-3))])
+def test_grouped_query_heads(cuda, op, kw, D):
+    """K/V with fewer heads than Q (8 query heads, 2 K/V heads): the oracle on
+    K/V repeated per query head, and bit-identical to passing those repeated
+    K/V to the kernel."""
+    B, H, Hkv, S = 1, 8, 2, 700
+    q, _, _ = gen(B, H, S, D, torch.bfloat16, seed=51)
+    _, k, v = gen(B, Hkv, S, D, torch.bfloat16, seed=52)
+    kr, vr = (x.repeat_interleave(H // Hkv, dim=1) for x in (k, v))
+    out = run(op, q, k, v, **kw)
+    check(out, oracle.run_op(op, q, kr, vr, **kw), f"{op} D={D}")
+    assert torch.equal(out, run(op, q, kr, vr, **kw))
