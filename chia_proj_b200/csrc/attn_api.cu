@@ -47,9 +47,12 @@ int derive(const chia_attn_params_t *p, Derived &out) {
   g.block = p->block;
   g.prefix = p->prefix < p->seqlen_kv ? p->prefix : p->seqlen_kv;
   g.dil = p->dilation;
+  g.seg = p->seq_offsets;
+  g.nseg = p->num_seqs;
   out.vdil = 1;
   const int64_t d = p->dilation;
-  if (d > 1 && g.block == 0 && g.prefix == 0 && g.sq % d == 0 && g.skv % d == 0) {
+  if (d > 1 && g.block == 0 && g.prefix == 0 && g.seg == nullptr && g.sq % d == 0 &&
+      g.skv % d == 0) {
     // i = i' d + r, j = j' d + r  =>  i - j = (i' - j') d
     g.sq /= d;
     g.skv /= d;
@@ -89,6 +92,13 @@ int validate(const chia_attn_params_t *p) {
     return CHIA_ERR_INVALID_ARGUMENT;
   if (p->heads_kv < 0 || (p->heads_kv > 0 && p->heads % p->heads_kv != 0))
     return CHIA_ERR_INVALID_ARGUMENT;
+  if (p->seq_offsets != nullptr) {  // packed sequences
+    if (p->num_seqs < 1 || p->num_seqs > (int64_t(1) << 30) || p->batch != 1 ||
+        p->seqlen_q != p->seqlen_kv || p->seqlen_q > 0x7fffffffLL)
+      return CHIA_ERR_INVALID_ARGUMENT;
+    if (p->block != 0 || p->prefix != 0 || p->dilation != 1) return CHIA_ERR_UNSUPPORTED;
+    if ((reinterpret_cast<uintptr_t>(p->seq_offsets) & 3u) != 0) return CHIA_ERR_MISALIGNED;
+  }
   // With S_q <= S_kv the diagonal key j = i is visible for every row under
   // every mask this ABI can describe, so no query row is left without keys.
   if (p->seqlen_q > p->seqlen_kv) return CHIA_ERR_UNSUPPORTED;
@@ -157,11 +167,11 @@ bool encode_map(CUtensorMap *map, const void *base, int dtype, int64_t D, int64_
 }
 
 // ----------------------------------------------------------------- dispatch
-template <int D, bool BF16, int KIND>
+template <int D, bool BF16, int KIND, bool SEG>
 int launch_one(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
                const chia::KernelArgs &a, int64_t nblocks, cudaStream_t stream) {
   using Cfg = chia::FmhaConfig<D>;
-  auto kern = chia::fmha_fwd_kernel<D, BF16, KIND>;
+  auto kern = chia::fmha_fwd_kernel<D, BF16, KIND, SEG>;
   static std::atomic<uint32_t> configured{0};  // bit per device ordinal (< 32)
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return CHIA_ERR_NO_DEVICE;
@@ -183,12 +193,12 @@ int launch_one(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &
 }
 
 // head_dim 128: CTA pairs with 2-SM UMMAs (fmha2_sm100.cuh)
-template <bool BF16, int KIND, bool MASKED>
+template <bool BF16, int KIND, bool MASKED, bool SEG>
 int launch_pair(const CUtensorMap &mq, const CUtensorMap &mkh, const CUtensorMap &mvh,
                 const CUtensorMap &mo, const chia::KernelArgs &a, int64_t nunits,
                 cudaStream_t stream) {
   using Cfg = chia::Fmha2Config<128>;
-  auto kern = chia::fmha2_fwd_kernel<128, BF16, KIND, MASKED>;
+  auto kern = chia::fmha2_fwd_kernel<128, BF16, KIND, MASKED, SEG>;
   static std::atomic<uint32_t> configured{0};
   static std::atomic<int> max_pairs[32];
   int dev = 0;
@@ -215,34 +225,34 @@ int launch_pair(const CUtensorMap &mq, const CUtensorMap &mkh, const CUtensorMap
   return cudaGetLastError() == cudaSuccess ? CHIA_OK : CHIA_ERR_LAUNCH;
 }
 
-template <bool BF16, bool MASKED>
+template <bool BF16, bool MASKED, bool SEG>
 int launch_pair_kind(int kind, const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
                      const CUtensorMap &mo, const chia::KernelArgs &a, int64_t nunits,
                      cudaStream_t s) {
   switch (kind) {
     case chia::KIND_SOFTMAX:
-      return launch_pair<BF16, chia::KIND_SOFTMAX, MASKED>(mq, mk, mv, mo, a, nunits, s);
+      return launch_pair<BF16, chia::KIND_SOFTMAX, MASKED, SEG>(mq, mk, mv, mo, a, nunits, s);
     case chia::KIND_SOFTCAP:
-      return launch_pair<BF16, chia::KIND_SOFTCAP, MASKED>(mq, mk, mv, mo, a, nunits, s);
+      return launch_pair<BF16, chia::KIND_SOFTCAP, MASKED, SEG>(mq, mk, mv, mo, a, nunits, s);
     case chia::KIND_ALIBI:
-      return launch_pair<BF16, chia::KIND_ALIBI, MASKED>(mq, mk, mv, mo, a, nunits, s);
+      return launch_pair<BF16, chia::KIND_ALIBI, MASKED, SEG>(mq, mk, mv, mo, a, nunits, s);
     case chia::KIND_SIGMOID:
-      return launch_pair<BF16, chia::KIND_SIGMOID, MASKED>(mq, mk, mv, mo, a, nunits, s);
+      return launch_pair<BF16, chia::KIND_SIGMOID, MASKED, SEG>(mq, mk, mv, mo, a, nunits, s);
     case chia::KIND_RELU:
-      return launch_pair<BF16, chia::KIND_RELU, MASKED>(mq, mk, mv, mo, a, nunits, s);
+      return launch_pair<BF16, chia::KIND_RELU, MASKED, SEG>(mq, mk, mv, mo, a, nunits, s);
   }
   return CHIA_ERR_INVALID_ARGUMENT;
 }
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool SEG>
 int launch_kind(int kind, const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
                 const chia::KernelArgs &a, int64_t nblocks, cudaStream_t s) {
   switch (kind) {
-    case chia::KIND_SOFTMAX: return launch_one<D, BF16, chia::KIND_SOFTMAX>(mq, mk, mv, a, nblocks, s);
-    case chia::KIND_SOFTCAP: return launch_one<D, BF16, chia::KIND_SOFTCAP>(mq, mk, mv, a, nblocks, s);
-    case chia::KIND_ALIBI: return launch_one<D, BF16, chia::KIND_ALIBI>(mq, mk, mv, a, nblocks, s);
-    case chia::KIND_SIGMOID: return launch_one<D, BF16, chia::KIND_SIGMOID>(mq, mk, mv, a, nblocks, s);
-    case chia::KIND_RELU: return launch_one<D, BF16, chia::KIND_RELU>(mq, mk, mv, a, nblocks, s);
+    case chia::KIND_SOFTMAX: return launch_one<D, BF16, chia::KIND_SOFTMAX, SEG>(mq, mk, mv, a, nblocks, s);
+    case chia::KIND_SOFTCAP: return launch_one<D, BF16, chia::KIND_SOFTCAP, SEG>(mq, mk, mv, a, nblocks, s);
+    case chia::KIND_ALIBI: return launch_one<D, BF16, chia::KIND_ALIBI, SEG>(mq, mk, mv, a, nblocks, s);
+    case chia::KIND_SIGMOID: return launch_one<D, BF16, chia::KIND_SIGMOID, SEG>(mq, mk, mv, a, nblocks, s);
+    case chia::KIND_RELU: return launch_one<D, BF16, chia::KIND_RELU, SEG>(mq, mk, mv, a, nblocks, s);
   }
   return CHIA_ERR_INVALID_ARGUMENT;
 }
@@ -317,7 +327,8 @@ const char *chia_attn_status_string(int status) {
 }
 
 int64_t chia_attn_visible_pairs(const chia_attn_params_t *p) {
-  if (p == nullptr || p->seqlen_q < 0 || p->seqlen_kv < 0 || p->win_left < -1 ||
+  if (p == nullptr || p->seq_offsets != nullptr || p->seqlen_q < 0 || p->seqlen_kv < 0 ||
+      p->win_left < -1 ||
       p->win_right < -1 || p->block < 0 || p->prefix < 0 || p->dilation < 1)
     return -1;
   return chia::visible_pairs(real_geom(p));
@@ -328,6 +339,7 @@ int chia_attn_tile_plan(const chia_attn_params_t *p, int64_t row0, int32_t tile_
                         uint64_t *full_mask) {
   if (p == nullptr || tile_m < 1 || tile_n < 1 || !tile_lo || !tile_hi || !full_mask || row0 < 0)
     return CHIA_ERR_INVALID_ARGUMENT;
+  if (p->seq_offsets != nullptr) return CHIA_ERR_UNSUPPORTED;  // device memory
   if (p->seqlen_q < 1 || p->seqlen_kv < 1 || p->win_left < -1 || p->win_right < -1 ||
       p->block < 0 || p->prefix < 0 || p->dilation < 1)
     return CHIA_ERR_INVALID_ARGUMENT;
@@ -409,15 +421,21 @@ int chia_attn_fwd(const chia_attn_params_t *p, void *stream) {
       return CHIA_ERR_LAUNCH;
     // every tile of every unit fully visible: the kernel without mask code
     const bool all_full = g.left < 0 && g.right < 0 && g.block == 0 && g.dil == 1 &&
-                          g.skv % 128 == 0;
+                          g.seg == nullptr && g.skv % 128 == 0;
     if (all_full)
-      return bf16 ? launch_pair_kind<true, false>(kind, mq, mkh, mv, mo, a, nunits, s)
-                  : launch_pair_kind<false, false>(kind, mq, mkh, mv, mo, a, nunits, s);
-    return bf16 ? launch_pair_kind<true, true>(kind, mq, mkh, mv, mo, a, nunits, s)
-                : launch_pair_kind<false, true>(kind, mq, mkh, mv, mo, a, nunits, s);
+      return bf16 ? launch_pair_kind<true, false, false>(kind, mq, mkh, mv, mo, a, nunits, s)
+                  : launch_pair_kind<false, false, false>(kind, mq, mkh, mv, mo, a, nunits, s);
+    if (g.seg != nullptr)  // packed sequences: the instantiation with the sequence lookup
+      return bf16 ? launch_pair_kind<true, true, true>(kind, mq, mkh, mv, mo, a, nunits, s)
+                  : launch_pair_kind<false, true, true>(kind, mq, mkh, mv, mo, a, nunits, s);
+    return bf16 ? launch_pair_kind<true, true, false>(kind, mq, mkh, mv, mo, a, nunits, s)
+                : launch_pair_kind<false, true, false>(kind, mq, mkh, mv, mo, a, nunits, s);
   }
-  return bf16 ? launch_kind<64, true>(kind, mq, mk, mv, a, nblocks, s)
-              : launch_kind<64, false>(kind, mq, mk, mv, a, nblocks, s);
+  if (g.seg != nullptr)
+    return bf16 ? launch_kind<64, true, true>(kind, mq, mk, mv, a, nblocks, s)
+                : launch_kind<64, false, true>(kind, mq, mk, mv, a, nblocks, s);
+  return bf16 ? launch_kind<64, true, false>(kind, mq, mk, mv, a, nblocks, s)
+              : launch_kind<64, false, false>(kind, mq, mk, mv, a, nblocks, s);
 }
 
 int chia_attn_fwd_noalloc(const chia_attn_params_t *p, void *stream) {

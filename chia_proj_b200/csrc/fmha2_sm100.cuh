@@ -154,8 +154,8 @@ __device__ __forceinline__ bool bounded_wait_cl(const WaitCtx &c, uint32_t bar, 
 
 // MASKED = false: every key tile of every unit is fully visible (the host
 // checks: no window, block or dilation and S_kv a multiple of 128), so the
-// element-wise mask code is left out of the kernel.
-template <int D, bool BF16, int KIND, bool MASKED>
+// element-wise mask code is left out of the kernel. SEG: packed sequences.
+template <int D, bool BF16, int KIND, bool MASKED, bool SEG>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THREADS, 1)
     fmha2_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_kh,
@@ -297,7 +297,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
         break;
       }
       UnitInfo U;
-      decode_unit<BM, BN>(u, args, U);
+      decode_unit<BM, BN, SEG>(u, args, U);
       // Q buffer qb held unit k-2, whose output is staged there: store it first
       const int qb = k & 1;
       if (k >= 2 && !store_o(qb, k - 2)) break;
@@ -376,7 +376,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       if (lane == 0) ptx::mbar_arrive(bar(C::BAR_UEMPTY + slot));
       if (u < 0) break;
       UnitInfo U;
-      decode_unit<BM, BN>(u, args, U);
+      decode_unit<BM, BN, SEG>(u, args, U);
       if (!wait(bar(C::BAR_QFULL + (k & 1)), (k >> 1) & 1)) break;
       dq = dq0 + (((k & 1) * C::Q_BYTES) >> 4);
       const int T = static_cast<int>(U.jhi - U.jlo);
@@ -470,18 +470,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       if (lane == 0) ptx::mbar_arrive_cluster(lbar(C::BAR_UEMPTY + slot));
       if (u < 0) break;
       UnitInfo U;
-      decode_unit<BM, BN>(u, args, U);
+      decode_unit<BM, BN, SEG>(u, args, U);
       const int w = static_cast<int>(rank);  // this CTA's query tile in the unit
       const int i = static_cast<int>(U.m0) + w * BM + row;
       const int64_t r0 = U.m0 + w * BM, r1 = r0 + BM - 1;
       int64_t blo64, bhi64;
-      row_band(g, i, blo64, bhi64);
+      row_band<SEG>(g, i, blo64, bhi64);
       const bool band_empty = bhi64 < blo64;
       const int blo = band_empty ? (1 << 30) : static_cast<int>(blo64);
       const uint32_t span = band_empty ? 0u : static_cast<uint32_t>(bhi64 - blo64);
       const float hp = args.head_param != nullptr ? args.head_param[U.h] : 1.0f;
       EpiConsts kc = make_epi_consts<KIND>(args, hp);
-      const FullTiles ft = full_tiles(g, r0, r1, BN);
+      const FullTiles ft = full_tiles<SEG>(g, r0, r1, BN);
       float m_run = -INFINITY, l_run = 0.f;
       bool ok = true, first_mine = true;
       const bool rev = reverse_tiles<KIND>(args, U);

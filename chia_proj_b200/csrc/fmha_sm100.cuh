@@ -436,7 +436,7 @@ struct UnitInfo {
 // Units are ordered head-major with the heaviest query block of a head first,
 // so the units in flight at any time share K/V in L2 and the light blocks
 // finish the schedule.
-template <int BM, int BN>
+template <int BM, int BN, bool SEG = false>
 __device__ __forceinline__ void decode_unit(int u, const KernelArgs &a, UnitInfo &U) {
   const int vh = u / a.n_qblocks;
   const int qb = a.n_qblocks - 1 - (u % a.n_qblocks);
@@ -448,7 +448,7 @@ __device__ __forceinline__ void decode_unit(int u, const KernelArgs &a, UnitInfo
   U.jhi = 0;
 #pragma unroll
   for (int w = 0; w < 2; ++w) {
-    tile_range(a.mask, U.m0 + w * BM, U.m0 + w * BM + BM - 1, BN, U.tlo[w], U.thi[w]);
+    tile_range<SEG>(a.mask, U.m0 + w * BM, U.m0 + w * BM + BM - 1, BN, U.tlo[w], U.thi[w]);
     if (U.tlo[w] < U.thi[w]) {
       U.jlo = imin64(U.jlo, U.tlo[w]);
       U.jhi = imax64(U.jhi, U.thi[w]);
@@ -461,7 +461,7 @@ __device__ __forceinline__ void decode_unit(int u, const KernelArgs &a, UnitInfo
 // balance; the last CTA to finish puts the counter back to zero), otherwise
 // CTA c runs units c, c + grid, c + 2 grid, ... . The unit index travels to the
 // other roles through a two-slot ring in shared memory.
-template <int D, bool BF16, int KIND>
+template <int D, bool BF16, int KIND, bool SEG>
 __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
     fmha_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                     const __grid_constant__ CUtensorMap tm_k,
@@ -555,7 +555,7 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
         ptx::mbar_arrive(bar(C::BAR_UFULL + slot));
         if (u < 0) break;
         UnitInfo U;
-        decode_unit<BM, BN>(u, args, U);
+        decode_unit<BM, BN, SEG>(u, args, U);
         // Q tiles: the previous unit's S MMAs must be done with the buffer
         if (k > 0 && !bounded_wait(wc, bar(C::BAR_QEMPTY), (k - 1) & 1)) break;
         uint32_t qbytes = 0;
@@ -643,7 +643,7 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
         ptx::mbar_arrive(bar(C::BAR_UEMPTY + slot));
         if (u < 0) break;
         UnitInfo U;
-        decode_unit<BM, BN>(u, args, U);
+        decode_unit<BM, BN, SEG>(u, args, U);
         if (!bounded_wait(wc, bar(C::BAR_Q), k & 1)) break;
         const int jlo = static_cast<int>(U.jlo), T = static_cast<int>(U.jhi - U.jlo);
         auto kpos = [&](int i) { return base + static_cast<uint32_t>(i == 0 ? 0 : 2 * i - 1); };
@@ -770,14 +770,14 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
       if (lane == 0) ptx::mbar_arrive(bar(C::BAR_UEMPTY + slot));
       if (u < 0) break;
       UnitInfo U;
-      decode_unit<BM, BN>(u, args, U);
+      decode_unit<BM, BN, SEG>(u, args, U);
       if (!U.wg_on(w)) continue;
 
       const int i = static_cast<int>(U.m0) + w * BM + row;
       const int64_t r0 = U.m0 + w * BM, r1 = r0 + BM - 1;
-      const FullTiles ft = full_tiles(g, r0, r1, BN);
+      const FullTiles ft = full_tiles<SEG>(g, r0, r1, BN);
       int64_t blo64, bhi64;
-      row_band(g, i, blo64, bhi64);
+      row_band<SEG>(g, i, blo64, bhi64);
       const bool band_empty = bhi64 < blo64;
       const int blo = band_empty ? (1 << 30) : static_cast<int>(blo64);
       const uint32_t span = band_empty ? 0u : static_cast<uint32_t>(bhi64 - blo64);

@@ -5,8 +5,10 @@
 // of
 //
 //   vis(i, j) = j < prefix  ||  ( lo(i) <= j <= hi(i)  &&  (i - j) % dil == 0 )
-//   lo(i) = max(0,        i - left  [left  >= 0],  block_start(i) [block > 0])
-//   hi(i) = min(S_kv - 1, i + right [right >= 0],  block_end(i)   [block > 0])
+//   lo(i) = max(0,        i - left  [left  >= 0],  block_start(i) [block > 0],
+//               seq_start(i) [packed sequences])
+//   hi(i) = min(S_kv - 1, i + right [right >= 0],  block_end(i)   [block > 0],
+//               seq_end(i) - 1 [packed sequences])
 //
 // lo(i) and hi(i) are non-decreasing in i, so the keys any row of a query
 // tile [r0, r1] can see lie in [lo(r0), hi(r1)] (plus [0, prefix)). That hull
@@ -29,12 +31,31 @@ struct MaskGeom {
   int64_t block;   // block size, 0 = none
   int64_t prefix;  // always-visible key prefix, already clipped to skv
   int64_t dil;     // dilation >= 1
+  // packed sequences: nseg + 1 cumulative offsets (device memory), or null
+  const int32_t *seg;
+  int64_t nseg;
 };
+
+// Sequence s of row i: seg[s] <= i < seg[s + 1] (binary search, seg[0] = 0).
+CHIA_HD int64_t seq_of(const MaskGeom &g, int64_t i) {
+  int64_t lo = 0, hi = g.nseg;
+  while (hi - lo > 1) {
+    const int64_t mid = (lo + hi) >> 1;
+    if (g.seg[mid] <= i)
+      lo = mid;
+    else
+      hi = mid;
+  }
+  return lo;
+}
 
 CHIA_HD int64_t imax64(int64_t a, int64_t b) { return a > b ? a : b; }
 CHIA_HD int64_t imin64(int64_t a, int64_t b) { return a < b ? a : b; }
 
-// Band [lo, hi] of row i (empty when lo > hi).
+// Band [lo, hi] of row i (empty when lo > hi). SEG: packed sequences (the
+// kernels are instantiated with and without, so calls without them carry no
+// sequence code at all).
+template <bool SEG = false>
 CHIA_HD void row_band(const MaskGeom &g, int64_t i, int64_t &lo, int64_t &hi) {
   lo = 0;
   hi = g.skv - 1;
@@ -45,17 +66,23 @@ CHIA_HD void row_band(const MaskGeom &g, int64_t i, int64_t &lo, int64_t &hi) {
     lo = imax64(lo, b0);
     hi = imin64(hi, b0 + g.block - 1);
   }
+  if (SEG) {
+    const int64_t s = seq_of(g, i);
+    lo = imax64(lo, g.seg[s]);
+    hi = imin64(hi, static_cast<int64_t>(g.seg[s + 1]) - 1);
+  }
 }
 
 // Key-tile range [tlo, thi) of width tn visited by query rows [r0, r1].
+template <bool SEG = false>
 CHIA_HD void tile_range(const MaskGeom &g, int64_t r0, int64_t r1, int tn, int64_t &tlo,
                         int64_t &thi) {
   tlo = thi = 0;
   if (r1 > g.sq - 1) r1 = g.sq - 1;
   if (r0 > r1 || g.skv <= 0) return;
   int64_t lo0, hi0, lo1, hi1;
-  row_band(g, r0, lo0, hi0);
-  row_band(g, r1, lo1, hi1);
+  row_band<SEG>(g, r0, lo0, hi0);
+  row_band<SEG>(g, r1, lo1, hi1);
   int64_t lo = lo0, hi = hi1;
   const bool band_empty = lo > hi;
   if (g.prefix > 0) {
@@ -95,6 +122,7 @@ struct FullTiles {
   }
 };
 
+template <bool SEG = false>
 CHIA_HD FullTiles full_tiles(const MaskGeom &g, int64_t r0, int64_t r1, int tn) {
   if (r1 > g.sq - 1) r1 = g.sq - 1;
   FullTiles f;
@@ -103,8 +131,8 @@ CHIA_HD FullTiles full_tiles(const MaskGeom &g, int64_t r0, int64_t r1, int tn) 
   f.band_lo = f.band_hi = 0;
   if (g.dil == 1) {
     int64_t lo_last, hi_last, lo_first, hi_first;
-    row_band(g, r1, lo_last, hi_last);
-    row_band(g, r0, lo_first, hi_first);
+    row_band<SEG>(g, r1, lo_last, hi_last);
+    row_band<SEG>(g, r0, lo_first, hi_first);
     // lo(r1) <= t tn  and  t tn + tn - 1 <= hi(r0)
     f.band_lo = static_cast<int32_t>((imax64(lo_last, 0) + tn - 1) / tn);
     f.band_hi = static_cast<int32_t>(imax64(hi_first + 1, 0) / tn);

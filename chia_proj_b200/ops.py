@@ -156,7 +156,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
               scale: Optional[float] = None, softcap: float = 30.0,
               head_param: Optional[Union[torch.Tensor, Sequence[float]]] = None,
               sig_bias: float = 0.0, out_scale: float = 1.0,
-              out: Optional[torch.Tensor] = None, schedule: str = "dynamic") -> torch.Tensor:
+              out: Optional[torch.Tensor] = None, schedule: str = "dynamic",
+              cu_seqlens=None) -> torch.Tensor:
     """Generic forward attention: ``norm(mask(mod(q.k * scale))) @ v``.
 
     ``q, k, v``: CUDA tensors ``[B, H, S, D]`` (bf16 / fp16; fp32 computed as
@@ -166,6 +167,12 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     or logit multipliers (``mod="temp"``), one per head. ``schedule``:
     ``"dynamic"`` balances work units over the SMs with a per-device
     workspace; ``"static"`` assigns them round-robin and uses no workspace.
+    ``cu_seqlens``: packed variable-length sequences. ``q, k, v`` hold a
+    batch of 1 whose ``S`` tokens are the concatenated sequences, with
+    sequence ``s`` at tokens ``[cu_seqlens[s], cu_seqlens[s+1])``; a query
+    sees keys of its own sequence only (then ``mask``, which may not use a
+    block, prefix or dilation). A list or CPU tensor is checked and copied to
+    the device; a CUDA int32 tensor is used as given.
     """
     if schedule not in ("dynamic", "static"):
         raise ValueError(f"unknown schedule {schedule!r}")
@@ -205,6 +212,25 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
         if o.stride(-1) != 1 or any(s % 8 for s in o.stride()[:-1]) or o.data_ptr() % 16:
             raise ValueError("out must have unit last stride and 16-byte aligned rows")
 
+    seg = None
+    if cu_seqlens is not None:
+        if B != 1 or k.shape[2] != S:
+            raise ValueError("packed sequences need a batch of 1 and S_q == S_kv")
+        if mask.block or mask.prefix or mask.dilation != 1:
+            raise ValueError("packed sequences take window and causal masks only")
+        cu = cu_seqlens if isinstance(cu_seqlens, torch.Tensor) else torch.tensor(cu_seqlens)
+        if cu.dim() != 1 or cu.numel() < 2:
+            raise ValueError("cu_seqlens must be 1-D with at least two offsets")
+        if cu.device.type == "cuda":
+            if cu.dtype != torch.int32 or cu.device != dev:
+                raise ValueError("a CUDA cu_seqlens must be int32 on the device of q")
+            seg = cu.contiguous()
+        else:
+            c = [int(x) for x in cu.tolist()]
+            if c[0] != 0 or c[-1] != S or any(b < a for a, b in zip(c, c[1:])):
+                raise ValueError(f"cu_seqlens must rise from 0 to S={S}")
+            seg = torch.tensor(c, dtype=torch.int32, device=dev)
+
     hp = None
     if mod in ("alibi", "temp"):
         hp = (_cached_default(mod, H, dev) if head_param is None
@@ -229,6 +255,9 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     p.win_left, p.win_right = mask.left, mask.right
     p.block, p.prefix, p.dilation = mask.block, mask.prefix, mask.dilation
     p.status = _status_word(dev).data_ptr()
+    if seg is not None:
+        p.seq_offsets = seg.data_ptr()
+        p.num_seqs = seg.numel() - 1
     # One workspace per device: calls on different streams of one device would
     # race on it, so only the current stream of the device is used here.
     p.workspace = _workspace(dev).data_ptr() if schedule == "dynamic" else None
@@ -245,29 +274,33 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
 # the ten reference operators (extra_bench.py:51-62)
 # ---------------------------------------------------------------------------
 def softcap_gemma2(q, k, v, *, cap: float = 30.0, causal: bool = True,
-                   scale: Optional[float] = None):
+                   scale: Optional[float] = None, cu_seqlens=None):
     """Gemma-2 softcap: ``softmax(cap*tanh(s/cap))`` (``extra_bench.py:60``)."""
     return attention(q, k, v, mod="softcap", softcap=cap, mask=CAUSAL if causal else FULL,
-                     scale=scale)
+                     scale=scale, cu_seqlens=cu_seqlens)
 
 
-def bias_sliding_window(q, k, v, *, window: int = 256, scale: Optional[float] = None):
+def bias_sliding_window(q, k, v, *, window: int = 256, scale: Optional[float] = None,
+                        cu_seqlens=None):
     """Causal window ``(j<=i)&(i-j<window)`` (``extra_bench.py:61``)."""
     if window < 1:
         raise ValueError("window must be >= 1")
-    return attention(q, k, v, mask=Mask(left=window - 1, right=0), scale=scale)
+    return attention(q, k, v, mask=Mask(left=window - 1, right=0), scale=scale,
+                     cu_seqlens=cu_seqlens)
 
 
-def bias_local(q, k, v, *, window: int = 256, scale: Optional[float] = None):
+def bias_local(q, k, v, *, window: int = 256, scale: Optional[float] = None, cu_seqlens=None):
     """Bidirectional band ``|i-j|<window`` (``extra_bench.py:57``)."""
     if window < 1:
         raise ValueError("window must be >= 1")
-    return attention(q, k, v, mask=Mask(left=window - 1, right=window - 1), scale=scale)
+    return attention(q, k, v, mask=Mask(left=window - 1, right=window - 1), scale=scale,
+                     cu_seqlens=cu_seqlens)
 
 
-def bias_alibi(q, k, v, *, slopes=None, scale: Optional[float] = None):
+def bias_alibi(q, k, v, *, slopes=None, scale: Optional[float] = None, cu_seqlens=None):
     """ALiBi ``s + slope_h*(j-i)``, causal (``extra_bench.py:47-50``); default slopes h+1."""
-    return attention(q, k, v, mod="alibi", head_param=slopes, mask=CAUSAL, scale=scale)
+    return attention(q, k, v, mod="alibi", head_param=slopes, mask=CAUSAL, scale=scale,
+                     cu_seqlens=cu_seqlens)
 
 
 def bias_block_diagonal(q, k, v, *, block: int = 512, causal: bool = True,
@@ -293,27 +326,28 @@ def bias_prefix_lm(q, k, v, *, prefix: int = 256, scale: Optional[float] = None)
     return attention(q, k, v, mask=Mask(left=-1, right=0, prefix=prefix), scale=scale)
 
 
-def temp_perhead(q, k, v, *, temps=None, scale: Optional[float] = None):
+def temp_perhead(q, k, v, *, temps=None, scale: Optional[float] = None, cu_seqlens=None):
     """``s*TEMP[h]``, causal (``extra_bench.py:35,54``); default TEMP ``0.5+h/H``.
 
     ``temps`` multiplies the logits like the reference's TEMP; a temperature
     tau dividing them is ``temps = 1/tau``.
     """
-    return attention(q, k, v, mod="temp", head_param=temps, mask=CAUSAL, scale=scale)
+    return attention(q, k, v, mod="temp", head_param=temps, mask=CAUSAL, scale=scale,
+                     cu_seqlens=cu_seqlens)
 
 
 def sigmoid_attn(q, k, v, *, causal: bool = True, bias: float = 0.0,
-                 scale: Optional[float] = None):
+                 scale: Optional[float] = None, cu_seqlens=None):
     """``sigmoid(s+bias)*mask @ v``, mask after the sigmoid (``sigmoid_fix.py:34-40``)."""
     return attention(q, k, v, norm="sigmoid", sig_bias=bias, mask=CAUSAL if causal else FULL,
-                     scale=scale)
+                     scale=scale, cu_seqlens=cu_seqlens)
 
 
 def relu_attn(q, k, v, *, causal: bool = True, out_scale: float = 1.0,
-              scale: Optional[float] = None):
+              scale: Optional[float] = None, cu_seqlens=None):
     """``relu(s)*mask @ v * out_scale`` (``extra_bench.py:44``)."""
     return attention(q, k, v, norm="relu", out_scale=out_scale,
-                     mask=CAUSAL if causal else FULL, scale=scale)
+                     mask=CAUSAL if causal else FULL, scale=scale, cu_seqlens=cu_seqlens)
 
 
 OPS = {

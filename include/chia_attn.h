@@ -56,7 +56,7 @@ extern "C" {
 #define CHIA_API
 #endif
 
-#define CHIA_ATTN_ABI_VERSION 2
+#define CHIA_ATTN_ABI_VERSION 3
 
 /* Size of the optional scheduler workspace (bytes). */
 #define CHIA_ATTN_WORKSPACE_BYTES 256
@@ -140,6 +140,16 @@ typedef struct chia_attn_params {
    * workspace must not run concurrently on the GPU. NULL selects a static
    * round-robin schedule (no scratch memory at all). */
   void *workspace;
+
+  /* Variable-length packed sequences: NULL, or a device int32 array of
+   * num_seqs + 1 cumulative offsets (0 = offsets[0] <= ... <=
+   * offsets[num_seqs] = seqlen_q; the array is read on the device only). Sequence s occupies rows and keys [offsets[s], offsets[s+1])
+   * of a batch of 1 with seqlen_q == seqlen_kv, and query i sees only keys of
+   * its own sequence (then the window rules above, with the same i - j).
+   * Requires block == 0, prefix == 0, dilation == 1. No counterpart in the
+   * reference, whose operators take one fixed length per batch. */
+  const int32_t *seq_offsets;
+  int64_t num_seqs;
 } chia_attn_params_t;
 
 /* Forward attention on `stream` (cudaStream_t; NULL = legacy default
@@ -178,14 +188,16 @@ CHIA_API int chia_attn_fwd_noalloc(const chia_attn_params_t *params, void *strea
 
 /* Number of visible (i, j) pairs of the mask described by params for one
  * (batch, head) pair -- the mask-aware FLOP count is 4 * D * pairs * B * H.
- * Host-only integer arithmetic; needs no GPU. Returns -1 on bad params. */
+ * Host-only integer arithmetic; needs no GPU. Returns -1 on bad params and
+ * for packed sequences (seq_offsets is device memory). */
 CHIA_API int64_t chia_attn_visible_pairs(const chia_attn_params_t *params);
 
 /* Key-tile plan of one query tile, the schedule the kernel runs. For query
  * rows [row0, row0 + tile_m) writes the first and one-past-last key tile of
  * width tile_n it visits and, into full_mask (bit t set = tile t needs no
  * element-wise masking; up to 64 tiles), which of them are unmasked.
- * Host-only; lets tests check the schedule without a GPU. Returns status. */
+ * Host-only; lets tests check the schedule without a GPU. Returns status
+ * (CHIA_ERR_UNSUPPORTED for packed sequences). */
 CHIA_API int chia_attn_tile_plan(const chia_attn_params_t *params, int64_t row0,
                         int32_t tile_m, int32_t tile_n, int64_t *tile_lo,
                         int64_t *tile_hi, uint64_t *full_mask);

@@ -22,5 +22,6 @@ from .eager import (  # noqa: F401
     OPS,
     reference_masks,
     run_op,
+    run_varlen,
     visible_pairs_dense,
 )

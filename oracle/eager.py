@@ -226,6 +226,20 @@ def run_op(op: str, q, k, v, **params) -> torch.Tensor:
     return OPS[op](q.cpu(), k.cpu(), v.cpu(), **params)
 
 
+def run_varlen(op: str, q, k, v, cu_seqlens, **params) -> torch.Tensor:
+    """Packed variable-length sequences: ``q, k, v`` are ``[1, H, S, D]`` whose
+    tokens are the concatenated sequences, sequence ``s`` at
+    ``[cu_seqlens[s], cu_seqlens[s+1])``. No counterpart in the reference (its
+    operators take one length per batch); the meaning is the reference
+    operator applied to each sequence on its own, which is what this does."""
+    cu = [int(x) for x in (cu_seqlens.tolist() if hasattr(cu_seqlens, "tolist") else cu_seqlens)]
+    out = torch.zeros(q.shape, dtype=torch.float32)
+    for a, b in zip(cu, cu[1:]):
+        if b > a:
+            out[:, :, a:b] = run_op(op, q[:, :, a:b], k[:, :, a:b], v[:, :, a:b], **params)
+    return out
+
+
 def visible_pairs_dense(maskfn: Callable, S: int) -> int:
     """Count visible (i, j) pairs of a reference mask by dense evaluation (small S)."""
     i = _rows(0, S)

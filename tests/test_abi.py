@@ -97,6 +97,16 @@ def _valid_params():
     (lambda p: setattr(p, "scale", float("nan")), 1),
     (lambda p: setattr(p, "heads_kv", 3), 1),    # 4 query heads, 3 K/V heads
     (lambda p: setattr(p, "heads_kv", -1), 1),
+    # packed sequences: batch must be 1 ...
+    (lambda p: (setattr(p, "seq_offsets", 0x20000), setattr(p, "num_seqs", 2)), 1),
+    # ... a prefix (or block, dilation) is not supported with them ...
+    (lambda p: (setattr(p, "batch", 1), setattr(p, "seq_offsets", 0x20000),
+                setattr(p, "num_seqs", 2), setattr(p, "prefix", 8)), 2),
+    # ... the offsets are int32 ...
+    (lambda p: (setattr(p, "batch", 1), setattr(p, "seq_offsets", 0x20002),
+                setattr(p, "num_seqs", 2)), 3),
+    (lambda p: (setattr(p, "batch", 1), setattr(p, "seq_offsets", 0x20000),
+                setattr(p, "num_seqs", 0)), 1),
 ])
 def test_argument_errors_are_reported_before_launch(lib, mutate, code):
     p = _valid_params()
@@ -112,6 +122,12 @@ def test_host_helpers_reject_bad_masks(lib):
     lo, hi, bits = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_uint64()
     assert lib.chia_attn_tile_plan(ctypes.byref(p), 0, 128, 128, ctypes.byref(lo),
                                    ctypes.byref(hi), ctypes.byref(bits)) == 1
+    # packed-sequence offsets live in device memory: the host helpers decline
+    p = _valid_params()
+    p.batch, p.seq_offsets, p.num_seqs = 1, 0x20000, 2
+    assert lib.chia_attn_visible_pairs(ctypes.byref(p)) == -1
+    assert lib.chia_attn_tile_plan(ctypes.byref(p), 0, 128, 128, ctypes.byref(lo),
+                                   ctypes.byref(hi), ctypes.byref(bits)) == 2
 
 
 def test_python_api_has_no_cpu_fallback(lib):

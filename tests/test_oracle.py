@@ -75,3 +75,17 @@ def test_oracle_row_blocking_is_invisible():
     a = eager._eval(q, k, v, maskfn=eager.reference_masks()["causal"], row_block=7)
     b = eager._eval(q, k, v, maskfn=eager.reference_masks()["causal"], row_block=1024)
     torch.testing.assert_close(a, b, rtol=1e-6, atol=1e-6)
+
+
+def test_varlen_oracle_is_the_operator_per_sequence():
+    """Packed sequences: each sequence's output is the operator on that
+    sequence alone, so tokens of other sequences do not affect it."""
+    g = torch.Generator().manual_seed(3)
+    q, k, v = (torch.randn(1, 2, 50, 16, generator=g) for _ in range(3))
+    cu = [0, 20, 20, 50]
+    out = oracle.run_varlen("softcap_gemma2", q, k, v, cu)
+    alone = oracle.run_op("softcap_gemma2", q[:, :, 20:], k[:, :, 20:], v[:, :, 20:])
+    assert torch.equal(out[:, :, 20:], alone)
+    k2 = k.clone()
+    k2[:, :, :20] += 5.0
+    assert torch.equal(oracle.run_varlen("softcap_gemma2", q, k2, v, cu)[:, :, 20:], out[:, :, 20:])

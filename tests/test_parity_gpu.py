@@ -312,3 +312,38 @@ def test_grouped_query_heads(cuda, op, kw, D):
     out = run(op, q, k, v, **kw)
     check(out, oracle.run_op(op, q, kr, vr, **kw), f"{op} D={D}")
     assert torch.equal(out, run(op, q, kr, vr, **kw))
+
+
+# ------------------------------------------------ packed variable-length sequences
+VARLEN_OFFSETS = [0, 100, 400, 417, 1017, 1017, 1272]  # includes an empty sequence
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("op,kw", [("softcap_gemma2", {}), ("bias_sliding_window", {}),
+                                   ("bias_local", dict(window=64)), ("bias_alibi", {}),
+                                   ("temp_perhead", {}),
+                                   ("sigmoid_attn", dict(causal=False)),
+                                   ("relu_attn", dict(out_scale=1e-2))])
+def test_packed_sequences_match_per_sequence_oracle(cuda, op, kw, D):
+    """cu_seqlens: every sequence attends only to itself, equal to the
+    reference operator applied to each sequence alone."""
+    S = VARLEN_OFFSETS[-1]
+    q, k, v = gen(1, 3, S, D, torch.bfloat16, seed=61)
+    out = run(op, q, k, v, cu_seqlens=VARLEN_OFFSETS, **kw)
+    check(out, oracle.run_varlen(op, q, k, v, VARLEN_OFFSETS, **kw), f"{op} D={D}")
+
+
+def test_packed_sequences_device_offsets_and_isolation(cuda):
+    """int32 offsets already on the device give the same result, and keys of
+    other sequences do not change a sequence's output (bit-exact)."""
+    S = VARLEN_OFFSETS[-1]
+    dev = torch.device("cuda", 0)
+    q, k, v = (t.to(dev) for t in gen(1, 2, S, 128, torch.bfloat16, seed=62))
+    cu = torch.tensor(VARLEN_OFFSETS, dtype=torch.int32, device=dev)
+    a = cp.softcap_gemma2(q, k, v, cu_seqlens=VARLEN_OFFSETS)
+    assert torch.equal(a, cp.softcap_gemma2(q, k, v, cu_seqlens=cu))
+    k2, v2 = k.clone(), v.clone()
+    k2[:, :, :400] = torch.randn_like(k2[:, :, :400]) * 3
+    v2[:, :, :400] = torch.randn_like(v2[:, :, :400]) * 3
+    b = cp.softcap_gemma2(q, k2, v2, cu_seqlens=cu)
+    assert torch.equal(a[:, :, 400:], b[:, :, 400:])
