@@ -585,8 +585,12 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
       for (int s = 0; s < NKV; ++s)
         if (last_item[s] >= 0)
           bounded_wait(wc, bar(C::BAR_KVFULL + s), (last_item[s] / NKV) & 1, false);
-    } else if (warp == C::MMA_WARP && lane == 0) {
+    } else if (warp == C::MMA_WARP) {
       // =========================== UMMA issuer ===========================
+      // The whole warp runs this loop in lockstep: readiness is tested by
+      // lane 0 and broadcast, so control flow stays uniform, the descriptors
+      // stay in uniform registers, and elect.sync picks the issuing lane.
+      auto uni = [&](bool x) { return __shfl_sync(0xffffffffu, x ? 1 : 0, 0) != 0; };
       constexpr uint32_t IDESC_QK = ptx::make_idesc_f16(BM, BN, BF16, false, false);
       constexpr uint32_t IDESC_PV = ptx::make_idesc_f16(BM, D, BF16, false, true);
       const uint32_t q_s = sbase + C::OFF_Q, p_s = sbase + C::OFF_P, kv_s = sbase + C::OFF_KV;
@@ -606,7 +610,7 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = ((kk >> 2) * C::CHUNK_Q_BYTES + (kk & 3) * 32) >> 4;
           const uint32_t offk = ((kk >> 2) * C::CHUNK_KV_BYTES + (kk & 3) * 32) >> 4;
-          ptx::umma_ss(d_tmem, a0 + off, b0 + offk, IDESC_QK, kk > 0 ? 1u : 0u);
+          ptx::umma_ss_warp(d_tmem, a0 + off, b0 + offk, IDESC_QK, kk > 0 ? 1u : 0u);
         }
       };
       auto issue_pv = [&](int w, int stage, bool first) {
@@ -616,12 +620,13 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint32_t offp = ((kk >> 2) * C::CHUNK_P_BYTES + (kk & 3) * 32) >> 4;
-          ptx::umma_ss(d_tmem, a0 + offp, b0 + ((kk * 2048) >> 4), IDESC_PV,
+          ptx::umma_ss_warp(d_tmem, a0 + offp, b0 + ((kk * 2048) >> 4), IDESC_PV,
                        (first && kk == 0) ? 0u : 1u);
         }
       };
 
-      Tracer tr(2);
+      Tracer trc(2);
+      auto tr = [&](int tag) { if (lane == 0) trc(tag); };
       // Event-driven issue: the thread polls every pending step of both query
       // tiles and issues whichever is ready, so neither softmax warpgroup
       // waits behind the other.
@@ -633,18 +638,20 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
       uint32_t base = 0;  // ring position of the current unit's first item
       uint32_t scnt[NQ] = {0, 0}, pcnt[NQ] = {0, 0}, units_w[NQ] = {0, 0};
       auto test_item = [&](uint32_t item) {
-        return ptx::mbar_test_wait(bar(C::BAR_KVFULL + item % NKV), (item / NKV) & 1);
+        return uni(ptx::mbar_test_wait(bar(C::BAR_KVFULL + item % NKV), (item / NKV) & 1));
       };
       bool ok = true;
       for (int k = 0; ok; ++k) {
         const int slot = k & 1;
-        if (!bounded_wait(wc, bar(C::BAR_UFULL + slot), (k >> 1) & 1)) break;
-        const int u = unit_ring[slot];
-        ptx::mbar_arrive(bar(C::BAR_UEMPTY + slot));
+        if (!__all_sync(0xffffffffu, bounded_wait(wc, bar(C::BAR_UFULL + slot), (k >> 1) & 1)))
+          break;
+        const int u = __shfl_sync(0xffffffffu, unit_ring[slot], 0);
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(bar(C::BAR_UEMPTY + slot));
         if (u < 0) break;
         UnitInfo U;
         decode_unit<BM, BN, SEG>(u, args, U);
-        if (!bounded_wait(wc, bar(C::BAR_Q), k & 1)) break;
+        if (!__all_sync(0xffffffffu, bounded_wait(wc, bar(C::BAR_Q), k & 1))) break;
         const int jlo = static_cast<int>(U.jlo), T = static_cast<int>(U.jhi - U.jlo);
         auto kpos = [&](int i) { return base + static_cast<uint32_t>(i == 0 ? 0 : 2 * i - 1); };
         auto vpos = [&](int i) {
@@ -668,10 +675,11 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
             if (sn[w] < hi[w]) {
               const uint32_t it = kpos(sn[w] - jlo);
               if (test_item(it) &&
-                  (scnt[w] == 0 || ptx::mbar_test_wait(bar(C::BAR_SFREE + w), (scnt[w] - 1) & 1))) {
+                  (scnt[w] == 0 ||
+                   uni(ptx::mbar_test_wait(bar(C::BAR_SFREE + w), (scnt[w] - 1) & 1)))) {
                 ptx::tc_fence_after();
                 issue_s(w, it % NKV);
-                ptx::umma_commit(bar(C::BAR_SFULL + w));
+                ptx::umma_commit_warp(bar(C::BAR_SFULL + w));
                 ++scnt[w];
                 ++sn[w];
                 progress = true;
@@ -681,15 +689,15 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
             if (pn[w] < hi[w]) {
               const uint32_t it = vpos(pn[w] - jlo);
               const bool first = pn[w] == lo[w];
-              if (ptx::mbar_test_wait(bar(C::BAR_PFULL + w), pcnt[w] & 1) && test_item(it) &&
+              if (uni(ptx::mbar_test_wait(bar(C::BAR_PFULL + w), pcnt[w] & 1)) && test_item(it) &&
                   (!first || units_w[w] == 0 ||
-                   ptx::mbar_test_wait(bar(C::BAR_OEMPTY + w), (units_w[w] - 1) & 1))) {
+                   uni(ptx::mbar_test_wait(bar(C::BAR_OEMPTY + w), (units_w[w] - 1) & 1)))) {
                 ptx::tc_fence_after();
                 issue_pv(w, it % NKV, first);
-                ptx::umma_commit(bar(C::BAR_PFREE + w));
+                ptx::umma_commit_warp(bar(C::BAR_PFREE + w));
                 ++pcnt[w];
                 if (pn[w] == hi[w] - 1) {
-                  ptx::umma_commit(bar(C::BAR_OFULL + w));
+                  ptx::umma_commit_warp(bar(C::BAR_OFULL + w));
                   ++units_w[w];
                 }
                 ++pn[w];
@@ -704,7 +712,7 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
             if ((user(0, t) && sn[0] <= t) || (user(1, t) && sn[1] <= t)) break;
             const uint32_t it = kpos(krel);
             if (!test_item(it)) break;  // an unused item must still have landed
-            ptx::umma_commit(bar(C::BAR_KVEMPTY + it % NKV));
+            ptx::umma_commit_warp(bar(C::BAR_KVEMPTY + it % NKV));
             ++krel;
           }
           while (vrel < T) {
@@ -712,11 +720,11 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
             if ((user(0, t) && pn[0] <= t) || (user(1, t) && pn[1] <= t)) break;
             const uint32_t it = vpos(vrel);
             if (!test_item(it)) break;
-            ptx::umma_commit(bar(C::BAR_KVEMPTY + it % NKV));
+            ptx::umma_commit_warp(bar(C::BAR_KVEMPTY + it % NKV));
             ++vrel;
           }
           if (!q_released && sn[0] >= hi[0] && sn[1] >= hi[1]) {
-            ptx::umma_commit(bar(C::BAR_QEMPTY));  // every S of this unit issued
+            ptx::umma_commit_warp(bar(C::BAR_QEMPTY));  // every S of this unit issued
             q_released = true;
           }
           if (krel >= T && vrel >= T && pn[0] >= hi[0] && pn[1] >= hi[1]) break;
@@ -724,12 +732,12 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
             idle_since = 0;
           } else {
             // nothing ready: back off briefly, bounded like every other wait
-            const uint64_t now = ptx::globaltimer_ns();
+            const uint64_t now = __shfl_sync(0xffffffffu, ptx::globaltimer_ns(), 0);
             if (idle_since == 0) idle_since = now;
-            if (*abort_flag) { ok = false; break; }
+            if (uni(*abort_flag != 0)) { ok = false; break; }
             if (now - idle_since > args.timeout_ns) {
               *abort_flag = 1;
-              if (args.status) atomicOr(args.status, 5 /* CHIA_ERR_DEVICE_TIMEOUT */);
+              if (args.status && lane == 0) atomicOr(args.status, 5 /* CHIA_ERR_DEVICE_TIMEOUT */);
               ok = false;
               break;
             }
@@ -739,7 +747,7 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
         base += 2 * static_cast<uint32_t>(T);
       }
       // Drain: all UMMAs issued by this thread complete before TMEM is freed.
-      ptx::umma_commit(bar(C::BAR_DRAIN));
+      ptx::umma_commit_warp(bar(C::BAR_DRAIN));
       bounded_wait(wc, bar(C::BAR_DRAIN), 0, false);
     }
     __syncwarp();

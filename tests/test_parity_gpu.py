@@ -347,3 +347,32 @@ def test_packed_sequences_device_offsets_and_isolation(cuda):
     v2[:, :, :400] = torch.randn_like(v2[:, :, :400]) * 3
     b = cp.softcap_gemma2(q, k2, v2, cu_seqlens=cu)
     assert torch.equal(a[:, :, 400:], b[:, :, 400:])
+
+
+# ------------------------------------------------ decode-shaped calls (S_q < S_kv)
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("Sq,Skv", [(1, 1000), (16, 1024), (200, 1000)])
+@pytest.mark.parametrize("norm", ["softmax", "sigmoid", "relu"])
+def test_decode_shaped_bottom_right_causal(cuda, norm, Sq, Skv, D):
+    """Few queries over a long key sequence, causal aligned at the end (query
+    i sits at position Skv - Sq + i: Mask(left=-1, right=Skv-Sq)), with
+    grouped K/V heads; against the oracle's generic evaluator."""
+    from oracle import eager
+    off = Skv - Sq
+    H, Hkv = 4, 2
+    q, _, _ = gen(2, H, Sq, D, torch.bfloat16, seed=71)
+    _, k, v = gen(2, Hkv, Skv, D, torch.bfloat16, seed=72)
+    kw = dict(sig_bias=-math.log(Skv)) if norm == "sigmoid" else \
+        dict(out_scale=1.0 / Skv) if norm == "relu" else {}
+    dev = torch.device("cuda", 0)
+    out = cp.attention(q.to(dev), k.to(dev), v.to(dev), norm=norm,
+                       mask=cp.Mask(left=-1, right=off), **kw)
+    kr, vr = (x.repeat_interleave(H // Hkv, dim=1) for x in (k, v))
+    if norm == "sigmoid":
+        ref = eager._eval(q, kr, vr, maskfn=lambda i, j: j <= i + off, norm="sigmoid",
+                          mod=lambda s, h, i, j: s + kw["sig_bias"])
+    else:
+        ref = eager._eval(q, kr, vr, maskfn=lambda i, j: j <= i + off, norm=norm)
+        if norm == "relu":
+            ref = ref * kw["out_scale"]
+    check(out, ref, f"{norm} Sq={Sq} Skv={Skv}")
