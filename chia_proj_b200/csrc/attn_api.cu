@@ -99,9 +99,8 @@ int validate(const chia_attn_params_t *p) {
     if (p->block != 0 || p->prefix != 0 || p->dilation != 1) return CHIA_ERR_UNSUPPORTED;
     if ((reinterpret_cast<uintptr_t>(p->seq_offsets) & 3u) != 0) return CHIA_ERR_MISALIGNED;
   }
-  // With S_q <= S_kv the diagonal key j = i is visible for every row under
-  // every mask this ABI can describe, so no query row is left without keys.
-  if (p->seqlen_q > p->seqlen_kv) return CHIA_ERR_UNSUPPORTED;
+  // S_q may exceed S_kv: a query row that sees no key (a window past the
+  // last key) gets a zero output row, and so do whole work units of them.
   if (p->seqlen_q > (int64_t(1) << 30) || p->seqlen_kv > (int64_t(1) << 30) ||
       p->heads > (int64_t(1) << 24) || p->batch > (int64_t(1) << 24))
     return CHIA_ERR_UNSUPPORTED;

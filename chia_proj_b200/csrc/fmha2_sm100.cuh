@@ -255,14 +255,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       ++n;
       return true;
     };
-    // O of the unit that used Q buffer b (this CTA's k_unit-th unit): once
-    // this CTA's softmax warps have staged it there, store this CTA's 128
-    // rows with TMA (rows past the sequence end are not written) and wait
-    // until the store has read the buffer.
+    // O of the unit that used Q buffer b: once this CTA's softmax warps have
+    // staged it there, store this CTA's 128 rows with TMA (rows past the
+    // sequence end are not written) and wait until the store has read the
+    // buffer. A unit whose rows see no key has its zeros written by the
+    // softmax warps directly and stages nothing, so the staging barrier's
+    // phases count the other units only (oph).
     UnitInfo uq[2];
-    auto store_o = [&](int b, int k_unit) -> bool {
-      if (!bounded_wait(wc, bar(C::BAR_OSTAGED + b), (k_unit >> 1) & 1)) return false;
+    uint32_t oph[2] = {0, 0};
+    auto store_o = [&](int b) -> bool {
       const UnitInfo &V = uq[b];
+      if (V.jhi == V.jlo) return true;
+      if (!bounded_wait(wc, bar(C::BAR_OSTAGED + b), oph[b])) return false;
+      oph[b] ^= 1u;
 #pragma unroll
       for (int c = 0; c < D / 64; ++c)
         ptx::tma_store_5d(&tm_o, sbase + C::OFF_Q + b * C::Q_BYTES + c * C::Q_CHUNK, c * 64,
@@ -300,16 +305,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       decode_unit<BM, BN, SEG>(u, args, U);
       // Q buffer qb held unit k-2, whose output is staged there: store it first
       const int qb = k & 1;
-      if (k >= 2 && !store_o(qb, k - 2)) break;
+      if (k >= 2 && !store_o(qb)) break;
       uq[qb] = U;
-      // this CTA's query tile (zero-filled by TMA when past the sequence end)
+      // this CTA's query tile (zero-filled by TMA when past the sequence end);
+      // a unit without key tiles only completes the barrier phase
       const uint32_t qfull = lbar(C::BAR_QFULL + qb);
-      ptx::mbar_arrive_expect_tx_remote(qfull, C::Q_BYTES);
+      if (U.jhi > U.jlo) {
+        ptx::mbar_arrive_expect_tx_remote(qfull, C::Q_BYTES);
 #pragma unroll
-      for (int c = 0; c < D / 64; ++c)
-        ptx::tma_load_5d_2sm(sbase + C::OFF_Q + qb * C::Q_BYTES + c * C::Q_CHUNK, &tm_q, qfull,
-                             c * 64, static_cast<int>(U.m0) + BM * static_cast<int>(rank), U.r_res,
-                             U.h, U.b);
+        for (int c = 0; c < D / 64; ++c)
+          ptx::tma_load_5d_2sm(sbase + C::OFF_Q + qb * C::Q_BYTES + c * C::Q_CHUNK, &tm_q, qfull,
+                               c * 64, static_cast<int>(U.m0) + BM * static_cast<int>(rank),
+                               U.r_res, U.h, U.b);
+      } else {
+        ptx::mbar_arrive_remote(qfull);
+      }
       bool ok = true;
       const bool rev = reverse_tiles<KIND>(args, U);
       for (int64_t k2 = 0; ok && k2 < U.jhi - U.jlo; ++k2)
@@ -319,7 +329,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
     // outputs of the last two units
     if (clean)
       for (int j = k_end >= 2 ? k_end - 2 : 0; j < k_end; ++j)
-        if (!store_o(j & 1, j)) break;
+        if (!store_o(j & 1)) break;
     ptx::bulk_wait_all();
     // Drain: this CTA's copies have landed once the even CTA released their
     // slots; on an abort the bounded waits below outlast any copy in flight.
@@ -377,6 +387,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       if (u < 0) break;
       UnitInfo U;
       decode_unit<BM, BN, SEG>(u, args, U);
+      if (U.jhi == U.jlo) continue;  // no key tiles: the softmax warps write zeros
       if (!wait(bar(C::BAR_QFULL + (k & 1)), (k >> 1) & 1)) break;
       dq = dq0 + (((k & 1) * C::Q_BYTES) >> 4);
       const int T = static_cast<int>(U.jhi - U.jlo);
@@ -474,6 +485,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       const int w = static_cast<int>(rank);  // this CTA's query tile in the unit
       const int i = static_cast<int>(U.m0) + w * BM + row;
       const int64_t r0 = U.m0 + w * BM, r1 = r0 + BM - 1;
+      if (U.jhi == U.jlo) {
+        // No row of the unit sees a key: its output is zero, written here
+        // (nothing is staged for the load thread to store).
+        if (i < g.sq) {
+          const int64_t real_row = static_cast<int64_t>(i) * args.vdil + U.r_res;
+          uint8_t *orow = reinterpret_cast<uint8_t *>(args.o) +
+                          2 * (U.b * args.o_sb + static_cast<int64_t>(U.h) * args.o_sh +
+                               real_row * args.o_ss + half * 64);
+#pragma unroll
+          for (int v4 = 0; v4 < 8; ++v4) ptx::st_global_v4(orow + v4 * 16, 0u, 0u, 0u, 0u);
+        }
+        continue;
+      }
       int64_t blo64, bhi64;
       row_band<SEG>(g, i, blo64, bhi64);
       const bool band_empty = bhi64 < blo64;
@@ -598,7 +622,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       } else {
         inv = 1.0f;
       }
-      if (!bounded_wait(wc, bar(C::BAR_OFULL), units & 1)) break;
+      if (!bounded_wait(wc, bar(C::BAR_OFULL), units & 1)) break;  // units with key tiles
       ptx::tc_fence_after();
       trs(14);
       uint32_t o[2][32];
@@ -620,11 +644,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
         for (int e = 0; e < 16; ++e)
           pk[c * 16 + e] = pack2<BF16>(__uint_as_float(o[c][2 * e]) * inv,
                                        __uint_as_float(o[c][2 * e + 1]) * inv);
-      const uint32_t qbuf = sbase + C::OFF_Q + (units & 1) * C::Q_BYTES + half * C::Q_CHUNK;
+      const uint32_t qbuf = sbase + C::OFF_Q + slot * C::Q_BYTES + half * C::Q_CHUNK;
       store_p_chunk(qbuf + row * 128, 0, row & 7, pk);
       ptx::fence_proxy_async_smem();  // visible to the TMA store
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar(C::BAR_OSTAGED + (units & 1)));
+      if (lane == 0) ptx::mbar_arrive(bar(C::BAR_OSTAGED + slot));
       trs(15);
       ++units;
     }

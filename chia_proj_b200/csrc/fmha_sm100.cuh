@@ -146,13 +146,16 @@ struct WaitCtx {
 // warpgroups (warp 0 / warp 4, lane 0), 2 MMA thread, 3 load thread.
 // ------------------------------------------------------------------------
 #ifdef CHIA_TRACE
+#ifndef CHIA_TRACE_BLOCK
+#define CHIA_TRACE_BLOCK 0
+#endif
 constexpr int kTraceEvents = 4096;
 __device__ unsigned long long g_chia_trace[4][kTraceEvents][2];
 struct Tracer {
   int role, n;
   __device__ __forceinline__ Tracer(int r) : role(r), n(0) {}
   __device__ __forceinline__ void operator()(int tag) {
-    if (blockIdx.x == 0 && n < kTraceEvents) {
+    if (blockIdx.x == CHIA_TRACE_BLOCK && n < kTraceEvents) {
       g_chia_trace[role][n][0] = static_cast<unsigned long long>(tag);
       g_chia_trace[role][n][1] = clock64();
       ++n;
@@ -454,6 +457,7 @@ __device__ __forceinline__ void decode_unit(int u, const KernelArgs &a, UnitInfo
       U.jhi = imax64(U.jhi, U.thi[w]);
     }
   }
+  if (U.jlo > U.jhi) U.jlo = U.jhi = 0;  // no row of the unit sees a key
 }
 
 // Persistent kernel: each CTA loops over work units. With a scheduler
@@ -573,7 +577,7 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
                                U.r_res, U.h, U.b);
         // K(jlo), then K(j+1) before V(j): ring position of K_i is 2i-1
         // (K_0 at 0), of V_i 2i+2, of the last V 2T-1 (T tiles in the unit)
-        bool ok = load_item(&tm_k, U.jlo, U);
+        bool ok = U.jlo == U.jhi || load_item(&tm_k, U.jlo, U);  // no items for a keyless unit
         for (int64_t j = U.jlo; ok && j < U.jhi; ++j) {
           if (j + 1 < U.jhi) ok = load_item(&tm_k, j + 1, U);
           ok = ok && load_item(&tm_v, j, U);
@@ -779,9 +783,20 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
       if (u < 0) break;
       UnitInfo U;
       decode_unit<BM, BN, SEG>(u, args, U);
-      if (!U.wg_on(w)) continue;
-
       const int i = static_cast<int>(U.m0) + w * BM + row;
+      if (!U.wg_on(w)) {
+        // no row of this query tile sees a key: its output is zero
+        if (i < g.sq) {
+          const int64_t real_row = static_cast<int64_t>(i) * args.vdil + U.r_res;
+          uint8_t *orow = reinterpret_cast<uint8_t *>(args.o) +
+                          2 * (U.b * args.o_sb + static_cast<int64_t>(U.h) * args.o_sh +
+                               real_row * args.o_ss);
+#pragma unroll
+          for (int v4 = 0; v4 < D / 8; ++v4) ptx::st_global_v4(orow + v4 * 16, 0u, 0u, 0u, 0u);
+        }
+        continue;
+      }
+
       const int64_t r0 = U.m0 + w * BM, r1 = r0 + BM - 1;
       const FullTiles ft = full_tiles<SEG>(g, r0, r1, BN);
       int64_t blo64, bhi64;

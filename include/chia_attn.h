@@ -103,7 +103,8 @@ typedef struct chia_attn_params {
 
   int64_t batch;     /* B                                                  */
   int64_t heads;     /* H                                                  */
-  int64_t seqlen_q;  /* S_q  (the reference operators use S_q == S_kv)     */
+  int64_t seqlen_q;  /* S_q  (the reference operators use S_q == S_kv; a
+                        row that sees no key gets a zero output row)    */
   int64_t seqlen_kv; /* S_kv                                               */
 
   /* device pointers, layout [B, H, S, D] with unit stride on D; strides in

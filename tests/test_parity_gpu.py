@@ -376,3 +376,34 @@ def test_decode_shaped_bottom_right_causal(cuda, norm, Sq, Skv, D):
         if norm == "relu":
             ref = ref * kw["out_scale"]
     check(out, ref, f"{norm} Sq={Sq} Skv={Skv}")
+
+
+# ------------------------------------------- work units whose rows see no key
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("norm", ["softmax", "sigmoid"])
+def test_keyless_units_write_zeros(cuda, norm, D):
+    """Query rows past the last visible key (S_q > S_kv, a window of 64):
+    rows 191.. see no key, so whole work units have no key tile. Their
+    output is zero -- written over a pre-filled buffer -- and the units in
+    between keep the pipeline's tile and buffer order intact."""
+    from oracle import eager
+    Sq, Skv, W = 1024, 128, 64
+    q, _, _ = gen(2, 3, Sq, D, torch.bfloat16, seed=81)
+    _, k, v = gen(2, 3, Skv, D, torch.bfloat16, seed=82)
+    kw = dict(sig_bias=-math.log(Skv)) if norm == "sigmoid" else {}
+    dev = torch.device("cuda", 0)
+    out = torch.full((2, 3, Sq, D), 7.0, dtype=torch.bfloat16, device=dev)
+    for schedule in ("dynamic", "static"):
+        cp.attention(q.to(dev), k.to(dev), v.to(dev), norm=norm, out=out,
+                     mask=cp.Mask(left=W - 1, right=0), schedule=schedule, **kw)
+        torch.cuda.synchronize()
+        maskfn = lambda i, j: (j <= i) & (j > i - W)
+        if norm == "sigmoid":
+            ref = eager._eval(q, k, v, maskfn=maskfn, norm="sigmoid",
+                              mod=lambda s, h, i, j: s + kw["sig_bias"])
+        else:
+            ref = torch.nan_to_num(eager._eval(q, k, v, maskfn=maskfn, norm=norm), nan=0.0)
+        got = out.float().cpu()
+        assert (got[:, :, Skv + W - 1:] == 0).all(), "keyless rows must be zero"
+        check(out, ref, f"{norm} D={D} {schedule}")
+        out.fill_(7.0)
