@@ -81,12 +81,18 @@ struct Fmha2Config {
   static constexpr int BAR_DRAIN = BAR_UEMPTY + 2;
   // exchange between the two softmax warps of one lane quadrant: [4 quad][2 slot]
   static constexpr int BAR_XCH = BAR_DRAIN + 1;
-  static constexpr int NUM_BARS = BAR_XCH + 8;
-  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // tmem base, abort, unit ring[2]
+  // per-CTA unit queue from the load thread to the softmax warps: [4] full / free
+  static constexpr int BAR_UQFULL = BAR_XCH + 8;
+  static constexpr int BAR_UQFREE = BAR_UQFULL + 4;
+  static constexpr int NUM_BARS = BAR_UQFREE + 4;
+  // tmem base, abort flag, unit ring [2], key tiles of the ring's units [2]
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   // row-max / row-sum exchange between the two softmax warpgroups:
   // float [2 parity][2 column half][128 rows]
-  static constexpr int OFF_XCH = OFF_MISC + 16;
-  static constexpr int SMEM_BYTES = OFF_XCH + 2 * 2 * 128 * 4;
+  static constexpr int OFF_XCH = OFF_MISC + 32;
+  // unit queue: 4 UnitSlot entries
+  static constexpr int OFF_UQ = OFF_XCH + 2 * 2 * 128 * 4;
+  static constexpr int SMEM_BYTES = OFF_UQ + 4 * 64;
   // No slack for aligning the base: the dynamic shared memory of a kernel
   // without static shared memory starts 1024-byte aligned (checked at run
   // time), and the second Q buffer needs the room.
@@ -97,9 +103,26 @@ struct Fmha2Config {
   static constexpr int LOAD_WARP = 9;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t TMEM_O = 384;
-  static constexpr int UNIT_CONSUMERS = 1 + 8 + 8 + 1;  // MMA, 2 x softmax warps, odd loader
+  static constexpr int UNIT_CONSUMERS = 2;  // of the ring: the MMA warp, the odd CTA's loader
   static_assert(SMEM_ALLOC <= 232448, "shared memory budget");
 };
+
+// One work unit as the load thread hands it to its CTA's softmax warps,
+// decoded once (the unit index alone costs the warps a few thousand cycles
+// of dependent integer arithmetic at every unit boundary).
+struct UnitSlot {
+  int32_t u;              // unit index (< 0: no more units)
+  int32_t tiles;          // key tiles of the unit (0: no row of it sees a key)
+  int32_t jlo;            // first key tile of the unit
+  int32_t rev;            // tiles visited last to first
+  int32_t r_res, h, b;    // residue class (dilation), query head, batch
+  int32_t pad;
+  int32_t m0;             // first query row of the unit
+  int32_t tlo, thi;       // key tiles [tlo, thi) of this CTA's query tile
+  FullTiles ft;           // key tiles this CTA's rows all see completely
+  float hp;               // per-head parameter (ALiBi slope, temperature)
+};
+static_assert(sizeof(UnitSlot) == 64, "unit slot layout");
 
 // Per-kind constants of the softmax / pointwise epilogue.
 template <int KIND>
@@ -178,6 +201,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + C::OFF_MISC);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + C::OFF_MISC + 4);
   volatile int *unit_ring = reinterpret_cast<volatile int *>(smem + C::OFF_MISC + 8);
+  volatile int *unit_tiles = reinterpret_cast<volatile int *>(smem + C::OFF_MISC + 16);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -208,6 +232,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       ptx::mbar_init(bar(C::BAR_UEMPTY + s), C::UNIT_CONSUMERS);
     }
     ptx::mbar_init(bar(C::BAR_DRAIN), 1);
+    for (int x = 0; x < 4; ++x) {
+      ptx::mbar_init(bar(C::BAR_UQFULL + x), 1);
+      ptx::mbar_init(bar(C::BAR_UQFREE + x), C::SOFTMAX_WARPS);
+    }
     for (int x = 0; x < 8; ++x) ptx::mbar_init(bar(C::BAR_XCH + x), 2);  // one arrive per warp
     *abort_flag = 0;
     ptx::fence_barrier_init();
@@ -287,22 +315,54 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
         u = args.sched ? atomicAdd(args.sched, 1)
                        : static_cast<int>(pair) + k * static_cast<int>(npairs);
         if (u >= args.n_units || u < 0) u = -1;
-        unit_ring[slot] = u;
-        ptx::st_shared_cluster_u32(ptx::mapa(sbase + C::OFF_MISC + 8 + 4 * slot, 1),
-                                   static_cast<uint32_t>(u));
-        ptx::mbar_arrive(bar(C::BAR_UFULL + slot));
-        ptx::mbar_arrive_cluster(ptx::mapa(bar(C::BAR_UFULL + slot), 1));
       } else {
         if (!bounded_wait_cl(wc, bar(C::BAR_UFULL + slot), (k >> 1) & 1)) break;
         u = unit_ring[slot];
         ptx::mbar_arrive_cluster(lbar(C::BAR_UEMPTY + slot));
       }
+      UnitInfo U;
+      int T = 0;
+      bool rev = false;
+      if (u >= 0) {
+        decode_unit<BM, BN, SEG>(u, args, U);
+        T = static_cast<int>(U.jhi - U.jlo);
+        rev = reverse_tiles<KIND>(args, U);
+      }
+      if (leader) {  // publish the unit and its key-tile count to both CTAs
+        unit_ring[slot] = u;
+        unit_tiles[slot] = T;
+        const uint32_t peer_misc = ptx::mapa(sbase + C::OFF_MISC, 1);
+        ptx::st_shared_cluster_u32(peer_misc + 8 + 4 * slot, static_cast<uint32_t>(u));
+        ptx::st_shared_cluster_u32(peer_misc + 16 + 4 * slot, static_cast<uint32_t>(T));
+        ptx::mbar_arrive(bar(C::BAR_UFULL + slot));
+        ptx::mbar_arrive_cluster(ptx::mapa(bar(C::BAR_UFULL + slot), 1));
+      }
+      // hand the unit, decoded, to this CTA's softmax warps
+      const int qs = k & 3;
+      if (k >= 4 && !bounded_wait(wc, bar(C::BAR_UQFREE + qs), ((k >> 2) & 1) ^ 1)) break;
+      {
+        UnitSlot *e = reinterpret_cast<UnitSlot *>(smem + C::OFF_UQ) + qs;
+        e->u = u;
+        e->tiles = T;
+        if (u >= 0) {
+          const int64_t r0 = U.m0 + BM * static_cast<int64_t>(rank);
+          e->jlo = static_cast<int32_t>(U.jlo);
+          e->rev = rev ? 1 : 0;
+          e->r_res = U.r_res;
+          e->h = U.h;
+          e->b = U.b;
+          e->m0 = static_cast<int32_t>(U.m0);
+          e->tlo = static_cast<int32_t>(U.tlo[rank]);
+          e->thi = static_cast<int32_t>(U.thi[rank]);
+          e->ft = full_tiles<SEG>(g, r0, r0 + BM - 1, BN);
+          e->hp = args.head_param != nullptr ? args.head_param[U.h] : 1.0f;
+        }
+      }
+      ptx::mbar_arrive(bar(C::BAR_UQFULL + qs));
       if (u < 0) {
         clean = true;
         break;
       }
-      UnitInfo U;
-      decode_unit<BM, BN, SEG>(u, args, U);
       // Q buffer qb held unit k-2, whose output is staged there: store it first
       const int qb = k & 1;
       if (k >= 2 && !store_o(qb)) break;
@@ -321,8 +381,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
         ptx::mbar_arrive_remote(qfull);
       }
       bool ok = true;
-      const bool rev = reverse_tiles<KIND>(args, U);
-      for (int64_t k2 = 0; ok && k2 < U.jhi - U.jlo; ++k2)
+      for (int64_t k2 = 0; ok && k2 < T; ++k2)
         ok = load_tile(rev ? U.jhi - 1 - k2 : U.jlo + k2, U);
       if (!ok) break;
     }
@@ -382,15 +441,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       if (!__all_sync(0xffffffffu, bounded_wait_cl(wc, bar(C::BAR_UFULL + slot), (k >> 1) & 1)))
         break;
       const int u = __shfl_sync(0xffffffffu, unit_ring[slot], 0);
+      const int T = __shfl_sync(0xffffffffu, unit_tiles[slot], 0);  // decoded by the loader
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar(C::BAR_UEMPTY + slot));
       if (u < 0) break;
-      UnitInfo U;
-      decode_unit<BM, BN, SEG>(u, args, U);
-      if (U.jhi == U.jlo) continue;  // no key tiles: the softmax warps write zeros
+      if (T == 0) continue;  // no key tiles: the softmax warps write zeros
       if (!wait(bar(C::BAR_QFULL + (k & 1)), (k >> 1) & 1)) break;
       dq = dq0 + (((k & 1) * C::Q_BYTES) >> 4);
-      const int T = static_cast<int>(U.jhi - U.jlo);
       // S of up to NSBUF tiles ahead
       const int pre = T < C::NSBUF ? T : C::NSBUF;
       for (int i = 0; i < pre; ++i) {
@@ -473,19 +530,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
     auto trs = [&](int tag) { if (tracing) tr(tag); };
     uint32_t cnt = 0;  // tiles seen (all tiles of every unit)
     uint32_t units = 0;
+    const int w = static_cast<int>(rank);  // this CTA's query tile in every unit
     for (int k = 0;; ++k) {
       const int slot = k & 1;
-      if (!bounded_wait_cl(wc, bar(C::BAR_UFULL + slot), (k >> 1) & 1)) break;
-      const int u = unit_ring[slot];
+      // the unit, as decoded by this CTA's load thread
+      const int qs = k & 3;
+      if (!bounded_wait(wc, bar(C::BAR_UQFULL + qs), (k >> 2) & 1)) break;
+      const UnitSlot U = reinterpret_cast<const UnitSlot *>(smem + C::OFF_UQ)[qs];
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive_cluster(lbar(C::BAR_UEMPTY + slot));
-      if (u < 0) break;
-      UnitInfo U;
-      decode_unit<BM, BN, SEG>(u, args, U);
-      const int w = static_cast<int>(rank);  // this CTA's query tile in the unit
-      const int i = static_cast<int>(U.m0) + w * BM + row;
-      const int64_t r0 = U.m0 + w * BM, r1 = r0 + BM - 1;
-      if (U.jhi == U.jlo) {
+      if (lane == 0) ptx::mbar_arrive(bar(C::BAR_UQFREE + qs));
+      if (U.u < 0) break;
+      const int i = U.m0 + w * BM + row;
+      if (U.tiles == 0) {
         // No row of the unit sees a key: its output is zero, written here
         // (nothing is staged for the load thread to store).
         if (i < g.sq) {
@@ -503,14 +559,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       const bool band_empty = bhi64 < blo64;
       const int blo = band_empty ? (1 << 30) : static_cast<int>(blo64);
       const uint32_t span = band_empty ? 0u : static_cast<uint32_t>(bhi64 - blo64);
-      const float hp = args.head_param != nullptr ? args.head_param[U.h] : 1.0f;
-      EpiConsts kc = make_epi_consts<KIND>(args, hp);
-      const FullTiles ft = full_tiles<SEG>(g, r0, r1, BN);
+      EpiConsts kc = make_epi_consts<KIND>(args, U.hp);
+      const FullTiles ft = U.ft;
       float m_run = -INFINITY, l_run = 0.f;
       bool ok = true, first_mine = true;
-      const bool rev = reverse_tiles<KIND>(args, U);
-      for (int64_t k2 = 0; k2 < U.jhi - U.jlo; ++k2, ++cnt) {
-        const int64_t t = rev ? U.jhi - 1 - k2 : U.jlo + k2;
+      for (int k2 = 0; k2 < U.tiles; ++k2, ++cnt) {
+        const int t = U.rev ? U.jlo + U.tiles - 1 - k2 : U.jlo + k2;
         const uint32_t buf = cnt % C::NSBUF;
         const uint32_t tS = tmem_base + lane_off + buf * 128 + half * 64;
         if (!bounded_wait(wc, bar(C::BAR_SFULL + buf), (cnt / C::NSBUF) & 1)) {
@@ -519,7 +573,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
         }
         trs(10);
         ptx::tc_fence_after();
-        if (U.active(w, t)) {
+        if (t >= U.tlo && t < U.thi) {  // this CTA's query tile sees key tile t
           uint32_t sr[2][32];
           ptx::tmem_ld32(tS, sr[0]);
           ptx::tmem_ld32(tS + 32, sr[1]);
