@@ -35,8 +35,10 @@
 // stores its own 64 columns of O. Warp 8 issues MMAs (the even CTA's lane 0;
 // both CTAs' warp 8 allocate TMEM), warp 9 loads.
 // Barriers that collect both CTAs live in the even CTA; the even CTA's
-// commits are multicast to both. The (dynamic) unit index is broadcast by the
-// even CTA's load thread into both CTAs' unit rings.
+// commits are multicast to both. The (dynamic) unit index and its key-tile
+// count are broadcast by the even CTA's load thread into both CTAs' unit
+// rings; each CTA's load thread also hands the decoded unit to its softmax
+// warps through a four-slot queue, so only the load thread decodes units.
 #pragma once
 #include "fmha_sm100.cuh"
 
