@@ -412,21 +412,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
     auto issue_s = [&](uint32_t buf, int stage) {
       const uint32_t d_tmem = tmem_base + buf * 128;
       const uint64_t b0 = dk + ((stage * C::STAGE_BYTES) >> 4);
+      static_assert(D / 16 == 8, "eight K-steps per S tile");
+      uint64_t ad[8], bd[8];
 #pragma unroll
-      for (int kk = 0; kk < D / 16; ++kk) {
-        const uint32_t offq = ((kk >> 2) * C::Q_CHUNK + (kk & 3) * 32) >> 4;
-        const uint32_t offk = ((kk >> 2) * C::KH_CHUNK + (kk & 3) * 32) >> 4;
-        ptx::umma_ss_2sm_warp(d_tmem, dq + offq, b0 + offk, IDESC_QK, kk > 0 ? 1u : 0u);
+      for (int kk = 0; kk < 8; ++kk) {
+        ad[kk] = dq + (((kk >> 2) * C::Q_CHUNK + (kk & 3) * 32) >> 4);
+        bd[kk] = b0 + (((kk >> 2) * C::KH_CHUNK + (kk & 3) * 32) >> 4);
       }
+      ptx::umma_ss_2sm_x8_warp(d_tmem, ad, bd, IDESC_QK, 0u);
     };
     auto issue_pv = [&](uint32_t buf, int stage, bool first) {
       const uint32_t d_tmem = tmem_base + C::TMEM_O;
       const uint32_t p_tmem = tmem_base + buf * 128;
       const uint64_t b0 = dv + ((stage * C::STAGE_BYTES) >> 4);
+      static_assert(BN / 16 == 8, "eight K-steps per PV tile");
+      uint32_t at[8];
+      uint64_t bd[8];
 #pragma unroll
-      for (int kk = 0; kk < BN / 16; ++kk)  // P of keys 16kk.. at column 8kk (+32 past key 64)
-        ptx::umma_ts_2sm_warp(d_tmem, p_tmem + kk * 8 + (kk >= 4 ? 32 : 0),
-                              b0 + ((kk * 2048) >> 4), IDESC_PV, (first && kk == 0) ? 0u : 1u);
+      for (int kk = 0; kk < 8; ++kk) {  // P of keys 16kk.. at column 8kk (+32 past key 64)
+        at[kk] = p_tmem + kk * 8 + (kk >= 4 ? 32 : 0);
+        bd[kk] = b0 + ((kk * 2048) >> 4);
+      }
+      ptx::umma_ts_2sm_x8_warp(d_tmem, at, bd, IDESC_PV, first ? 0u : 1u);
     };
     Tracer trc(2);
     auto tr = [&](int tag) { if (lane == 0) trc(tag); };

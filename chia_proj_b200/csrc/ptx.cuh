@@ -404,6 +404,51 @@ __device__ __forceinline__ void umma_ts_2sm_warp(uint32_t d_tmem, uint32_t a_tme
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Eight K-steps of one 2-SM UMMA chain under one elect.sync (the first
+// accumulates iff acc0, the others always): S = Q K^T from shared memory, or
+// O += P V with P in tensor memory.
+__device__ __forceinline__ void umma_ss_2sm_x8_warp(uint32_t d_tmem, const uint64_t (&a)[8],
+                                                    const uint64_t (&b)[8], uint32_t idesc,
+                                                    uint32_t acc0) {
+  asm volatile(
+      "{\n\t.reg .pred p, q, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %18, 0;\n\t"
+      "setp.eq.b32 q, %18, %18;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %9, %17, p;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %2, %10, %17, q;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %3, %11, %17, q;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %4, %12, %17, q;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %5, %13, %17, q;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %6, %14, %17, q;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %7, %15, %17, q;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], %8, %16, %17, q;\n\t}" ::"r"(d_tmem),
+      "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(a[4]), "l"(a[5]), "l"(a[6]), "l"(a[7]),
+      "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]),
+      "r"(idesc), "r"(acc0)
+      : "memory");
+}
+__device__ __forceinline__ void umma_ts_2sm_x8_warp(uint32_t d_tmem, const uint32_t (&a)[8],
+                                                    const uint64_t (&b)[8], uint32_t idesc,
+                                                    uint32_t acc0) {
+  asm volatile(
+      "{\n\t.reg .pred p, q, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %18, 0;\n\t"
+      "setp.eq.b32 q, %18, %18;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %9, %17, p;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%2], %10, %17, q;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%3], %11, %17, q;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%4], %12, %17, q;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%5], %13, %17, q;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%6], %14, %17, q;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%7], %15, %17, q;\n\t"
+      "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%8], %16, %17, q;\n\t}" ::"r"(d_tmem),
+      "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(a[4]), "r"(a[5]), "r"(a[6]), "r"(a[7]),
+      "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]), "l"(b[4]), "l"(b[5]), "l"(b[6]), "l"(b[7]),
+      "r"(idesc), "r"(acc0)
+      : "memory");
+}
 __device__ __forceinline__ void umma_commit_2sm_warp(uint32_t bar, uint16_t cta_mask) {
   asm volatile(
       "{\n\t.reg .pred e;\n\t"
