@@ -114,7 +114,9 @@ struct FmhaConfig {
   static constexpr int NUM_BARS = BAR_DRAIN + 1;
   // misc: [0] TMEM base, [1] abort flag, [2..3] unit ring
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
-  static constexpr int SMEM_BYTES = OFF_MISC + 16;
+  // the ring's two units as decoded by the load thread (UnitSlot2 each)
+  static constexpr int OFF_US = OFF_MISC + 16;
+  static constexpr int SMEM_BYTES = OFF_US + 2 * 96;
   static constexpr int SMEM_ALLOC = SMEM_BYTES + 1024;  // slack for 1024-byte alignment
   // 12 warps: warpgroups 0 and 1 = softmax (one query tile each), warpgroup 2
   // = MMA warp, load warp and two idle warps. setmaxnreg moves registers from
@@ -460,6 +462,21 @@ __device__ __forceinline__ void decode_unit(int u, const KernelArgs &a, UnitInfo
   if (U.jlo > U.jhi) U.jlo = U.jhi = 0;  // no row of the unit sees a key
 }
 
+// A work unit of the head_dim-64 kernel as its load thread hands it to the
+// MMA warp and the softmax warpgroups through the unit ring, decoded once
+// (decoding costs each reader a few thousand cycles of dependent integer work
+// at every unit boundary).
+struct UnitSlot2 {
+  int32_t jlo, jhi;        // key tiles of the unit
+  int32_t m0;              // first query row
+  int32_t r_res, h, b;     // residue class (dilation), query head, batch
+  int32_t tlo[2], thi[2];  // key tiles of each query tile (empty: lo == hi)
+  FullTiles ft[2];         // key tiles each query tile's rows all see completely
+  float hp;                // per-head parameter
+  int32_t pad[5];
+};
+static_assert(sizeof(UnitSlot2) == 96, "unit slot layout");
+
 // Persistent kernel: each CTA loops over work units. With a scheduler
 // workspace the load warp takes the next unit from a global counter (dynamic
 // balance; the last CTA to finish puts the counter back to zero), otherwise
@@ -556,10 +573,26 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
         int u = args.sched ? atomicAdd(args.sched, 1) : static_cast<int>(blockIdx.x) + k * static_cast<int>(gridDim.x);
         if (u >= args.n_units || u < 0) u = -1;
         unit_ring[slot] = u;
+        UnitInfo U;
+        if (u >= 0) {
+          decode_unit<BM, BN, SEG>(u, args, U);
+          UnitSlot2 *e = reinterpret_cast<UnitSlot2 *>(smem + C::OFF_US) + slot;
+          e->jlo = static_cast<int32_t>(U.jlo);
+          e->jhi = static_cast<int32_t>(U.jhi);
+          e->m0 = static_cast<int32_t>(U.m0);
+          e->r_res = U.r_res;
+          e->h = U.h;
+          e->b = U.b;
+#pragma unroll
+          for (int w = 0; w < NQ; ++w) {
+            e->tlo[w] = static_cast<int32_t>(U.tlo[w]);
+            e->thi[w] = static_cast<int32_t>(U.thi[w]);
+            e->ft[w] = full_tiles<SEG>(g, U.m0 + w * BM, U.m0 + w * BM + BM - 1, BN);
+          }
+          e->hp = args.head_param != nullptr ? args.head_param[U.h] : 1.0f;
+        }
         ptx::mbar_arrive(bar(C::BAR_UFULL + slot));
         if (u < 0) break;
-        UnitInfo U;
-        decode_unit<BM, BN, SEG>(u, args, U);
         // Q tiles: the previous unit's S MMAs must be done with the buffer
         if (k > 0 && !bounded_wait(wc, bar(C::BAR_QEMPTY), (k - 1) & 1)) break;
         uint32_t qbytes = 0;
@@ -650,13 +683,12 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
         if (!__all_sync(0xffffffffu, bounded_wait(wc, bar(C::BAR_UFULL + slot), (k >> 1) & 1)))
           break;
         const int u = __shfl_sync(0xffffffffu, unit_ring[slot], 0);
+        const UnitSlot2 U = reinterpret_cast<const UnitSlot2 *>(smem + C::OFF_US)[slot];
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(bar(C::BAR_UEMPTY + slot));
         if (u < 0) break;
-        UnitInfo U;
-        decode_unit<BM, BN, SEG>(u, args, U);
         if (!__all_sync(0xffffffffu, bounded_wait(wc, bar(C::BAR_Q), k & 1))) break;
-        const int jlo = static_cast<int>(U.jlo), T = static_cast<int>(U.jhi - U.jlo);
+        const int jlo = U.jlo, T = U.jhi - U.jlo;
         auto kpos = [&](int i) { return base + static_cast<uint32_t>(i == 0 ? 0 : 2 * i - 1); };
         auto vpos = [&](int i) {
           return base + static_cast<uint32_t>(i < T - 1 ? 2 * i + 2 : 2 * T - 1);
@@ -664,8 +696,8 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
         int sn[NQ], pn[NQ], lo[NQ], hi[NQ];
 #pragma unroll
         for (int w = 0; w < NQ; ++w) {
-          lo[w] = static_cast<int>(U.tlo[w]);
-          hi[w] = static_cast<int>(U.thi[w]);
+          lo[w] = U.tlo[w];
+          hi[w] = U.thi[w];
           sn[w] = pn[w] = lo[w];
         }
         auto user = [&](int w, int t) { return t >= lo[w] && t < hi[w]; };
@@ -778,13 +810,12 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
       const int slot = k & 1;
       if (!bounded_wait(wc, bar(C::BAR_UFULL + slot), (k >> 1) & 1)) break;
       const int u = unit_ring[slot];
+      const UnitSlot2 U = reinterpret_cast<const UnitSlot2 *>(smem + C::OFF_US)[slot];
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar(C::BAR_UEMPTY + slot));
       if (u < 0) break;
-      UnitInfo U;
-      decode_unit<BM, BN, SEG>(u, args, U);
-      const int i = static_cast<int>(U.m0) + w * BM + row;
-      if (!U.wg_on(w)) {
+      const int i = U.m0 + w * BM + row;
+      if (U.tlo[w] >= U.thi[w]) {
         // no row of this query tile sees a key: its output is zero
         if (i < g.sq) {
           const int64_t real_row = static_cast<int64_t>(i) * args.vdil + U.r_res;
@@ -797,16 +828,14 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
         continue;
       }
 
-      const int64_t r0 = U.m0 + w * BM, r1 = r0 + BM - 1;
-      const FullTiles ft = full_tiles<SEG>(g, r0, r1, BN);
+      const FullTiles ft = U.ft[w];
       int64_t blo64, bhi64;
       row_band<SEG>(g, i, blo64, bhi64);
       const bool band_empty = bhi64 < blo64;
       const int blo = band_empty ? (1 << 30) : static_cast<int>(blo64);
       const uint32_t span = band_empty ? 0u : static_cast<uint32_t>(bhi64 - blo64);
       // per-kind constants (log2 domain for the softmax kinds)
-      float hp = 1.0f;
-      if (args.head_param != nullptr) hp = args.head_param[U.h];
+      const float hp = U.hp;
       EpiConsts kc;
       kc.k_mul = score_scale * LOG2E;
       kc.k_cap = 0.f;
@@ -825,7 +854,7 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
 
       float m_run = -INFINITY, l_run = 0.f;
       bool ok = true;
-      for (int64_t t = U.tlo[w]; t < U.thi[w]; ++t, ++cnt) {
+      for (int t = U.tlo[w]; t < U.thi[w]; ++t, ++cnt) {
         if (!bounded_wait(wc, bar(C::BAR_SFULL + w), cnt & 1)) { ok = false; break; }
         trs(10);  // S ready
         ptx::tc_fence_after();
