@@ -584,11 +584,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
         ptx::tc_fence_after();
         if (t >= U.tlo && t < U.thi) {  // this CTA's query tile sees key tile t
           uint32_t sr[2][32];
-          ptx::tmem_ld32(tS, sr[0]);
-          ptx::tmem_ld32(tS + 32, sr[1]);
-          ptx::tmem_wait_ld();
-          ptx::reg_fence(sr[0]);
-          ptx::reg_fence(sr[1]);
+          if (SOFTMAX) {
+            ptx::tmem_ld32(tS, sr[0]);
+            ptx::tmem_ld32(tS + 32, sr[1]);
+            ptx::tmem_wait_ld();
+            ptx::reg_fence(sr[0]);
+            ptx::reg_fence(sr[1]);
+          }
           trs(11);
           const int kv0 = static_cast<int>(t) * BN + half * 64;  // key of column 0 of sr
           RowMask rm;
@@ -645,11 +647,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
             l_run += lsum;
           } else {
             if (mode == 0)
-              pointwise_tile<KIND, 0, BF16>(sr, kc, rm, sink);
+              pointwise_tmem64<KIND, 0, BF16>(tS, kc, rm);
             else if (mode == 1)
-              pointwise_tile<KIND, 1, BF16>(sr, kc, rm, sink);
+              pointwise_tmem64<KIND, 1, BF16>(tS, kc, rm);
             else
-              pointwise_tile<KIND, 2, BF16>(sr, kc, rm, sink);
+              pointwise_tmem64<KIND, 2, BF16>(tS, kc, rm);
           }
           first_mine = false;
           trs(12);

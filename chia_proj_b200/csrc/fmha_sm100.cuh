@@ -335,55 +335,80 @@ __device__ __forceinline__ float softmax_pass2(uint32_t (&sr)[NC][32], float m, 
 // (initial guess from the exponent-field complement 0x7EF311C7 - bits(y),
 // then two Newton steps r <- r (2 - y r); relative error about 2e-4, below
 // the 2^-9 rounding of the 16-bit P).
-template <int KIND, int MODE, bool BF16, class Sink, int NC = 4>
-__device__ __forceinline__ void pointwise_tile(uint32_t (&sr)[NC][32], const EpiConsts &k,
-                                               const RowMask &rm, const Sink &sink) {
-  static_assert(NC == 2 || NC == 4, "64 or 128 columns");
+// One 32-column chunk (src, columns col0..col0+31 of the tile) of the
+// pointwise kinds, as 16 packed pairs into pk[off .. off+15].
+template <int KIND, int MODE, bool BF16>
+__device__ __forceinline__ void pointwise_chunk(const uint32_t (&src)[32], int col0,
+                                                const EpiConsts &k, const RowMask &rm,
+                                                uint32_t (&pk)[32], int off) {
   const uint64_t K2 = ptx::f2(k.k_mul, k.k_mul);
   const uint64_t KB2 = ptx::f2(k.k_bias, k.k_bias);
   const uint64_t NEG1 = ptx::f2(-1.0f, -1.0f);
   const uint64_t TWO2 = ptx::f2(2.0f, 2.0f);
 #pragma unroll
+  for (int e = 0; e < 32; e += 2) {
+    const int col = col0 + e;
+    const uint64_t s2 = ptx::f2(__uint_as_float(src[e]), __uint_as_float(src[e + 1]));
+    float a, b;
+    if (KIND == KIND_RELU) {
+      ptx::f2_split(ptx::mul2(s2, K2), a, b);
+      if (MODE != 0) {
+        if (!col_visible<MODE>(rm, col)) a = 0.f;
+        if (!col_visible<MODE>(rm, col + 1)) b = 0.f;
+      }
+      pk[off + e / 2] = BF16 ? ptx::pack_bf16_relu(a, b) : ptx::pack_f16_relu(a, b);
+    } else {
+      // t = -(s*scale + bias) * log2(e), clamped so 2^t stays finite
+      float t0, t1;
+      ptx::f2_split(ptx::fma2(s2, K2, KB2), t0, t1);
+      const uint64_t e2 = ptx::f2(ptx::ex2(fminf(t0, 126.f)), ptx::ex2(fminf(t1, 126.f)));
+      const uint64_t ny = ptx::fma2(e2, NEG1, NEG1);  // -(1 + 2^t)
+      float y0, y1;
+      ptx::f2_split(ny, y0, y1);
+      uint64_t r = ptx::f2(__uint_as_float(0xFEF311C7u - __float_as_uint(y0)),
+                           __uint_as_float(0xFEF311C7u - __float_as_uint(y1)));
+      r = ptx::mul2(r, ptx::fma2(ny, r, TWO2));
+      r = ptx::mul2(r, ptx::fma2(ny, r, TWO2));
+      ptx::f2_split(r, a, b);
+      if (MODE != 0) {
+        if (!col_visible<MODE>(rm, col)) a = 0.f;
+        if (!col_visible<MODE>(rm, col + 1)) b = 0.f;
+      }
+      pk[off + e / 2] = pack2<BF16>(a, b);
+    }
+  }
+}
+
+template <int KIND, int MODE, bool BF16, class Sink, int NC = 4>
+__device__ __forceinline__ void pointwise_tile(uint32_t (&sr)[NC][32], const EpiConsts &k,
+                                               const RowMask &rm, const Sink &sink) {
+  static_assert(NC == 2 || NC == 4, "64 or 128 columns");
+#pragma unroll
   for (int h2 = 0; h2 < NC / 2; ++h2) {
     uint32_t pk[32];
 #pragma unroll
-    for (int cc = 0; cc < 2; ++cc) {
-      const int c = 2 * h2 + cc;
-#pragma unroll
-      for (int e = 0; e < 32; e += 2) {
-        const int col = c * 32 + e;
-        const uint64_t s2 = ptx::f2(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1]));
-        float a, b;
-        if (KIND == KIND_RELU) {
-          ptx::f2_split(ptx::mul2(s2, K2), a, b);
-          if (MODE != 0) {
-            if (!col_visible<MODE>(rm, col)) a = 0.f;
-            if (!col_visible<MODE>(rm, col + 1)) b = 0.f;
-          }
-          pk[cc * 16 + e / 2] = BF16 ? ptx::pack_bf16_relu(a, b) : ptx::pack_f16_relu(a, b);
-        } else {
-          // t = -(s*scale + bias) * log2(e), clamped so 2^t stays finite
-          float t0, t1;
-          ptx::f2_split(ptx::fma2(s2, K2, KB2), t0, t1);
-          const uint64_t e2 = ptx::f2(ptx::ex2(fminf(t0, 126.f)), ptx::ex2(fminf(t1, 126.f)));
-          const uint64_t ny = ptx::fma2(e2, NEG1, NEG1);  // -(1 + 2^t)
-          float y0, y1;
-          ptx::f2_split(ny, y0, y1);
-          uint64_t r = ptx::f2(__uint_as_float(0xFEF311C7u - __float_as_uint(y0)),
-                               __uint_as_float(0xFEF311C7u - __float_as_uint(y1)));
-          r = ptx::mul2(r, ptx::fma2(ny, r, TWO2));
-          r = ptx::mul2(r, ptx::fma2(ny, r, TWO2));
-          ptx::f2_split(r, a, b);
-          if (MODE != 0) {
-            if (!col_visible<MODE>(rm, col)) a = 0.f;
-            if (!col_visible<MODE>(rm, col + 1)) b = 0.f;
-          }
-          pk[cc * 16 + e / 2] = pack2<BF16>(a, b);
-        }
-      }
-    }
+    for (int cc = 0; cc < 2; ++cc)
+      pointwise_chunk<KIND, MODE, BF16>(sr[2 * h2 + cc], (2 * h2 + cc) * 32, k, rm, pk, cc * 16);
     sink(h2, pk);
   }
+}
+
+// Pointwise kinds on this thread's 64 columns of a TMEM S tile (2-SM
+// kernel): chunk 0 is transformed while chunk 1 is still being read from
+// tensor memory; P (64 keys) goes back over chunk 0's columns.
+template <int KIND, int MODE, bool BF16>
+__device__ __forceinline__ void pointwise_tmem64(uint32_t tS, const EpiConsts &k,
+                                                 const RowMask &rm) {
+  uint32_t s0[32], s1[32], pk[32];
+  ptx::tmem_ld32(tS, s0);
+  ptx::tmem_wait_ld();
+  ptx::reg_fence(s0);
+  ptx::tmem_ld32(tS + 32, s1);
+  pointwise_chunk<KIND, MODE, BF16>(s0, 0, k, rm, pk, 0);
+  ptx::tmem_wait_ld();
+  ptx::reg_fence(s1);
+  pointwise_chunk<KIND, MODE, BF16>(s1, 32, k, rm, pk, 16);
+  ptx::tmem_st32(tS, pk);
 }
 
 // D columns of O (from tO) of this thread's row *= alpha (lazy softmax
