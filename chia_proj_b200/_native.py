@@ -14,7 +14,7 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "_lib", "libchia_attn.so")
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 WORKSPACE_BYTES = 256
 NOALLOC_SCRATCH_BYTES = 256
 NOALLOC_MAX_UNITS = 1 << 30
@@ -79,6 +79,8 @@ class AttnParams(ctypes.Structure):
         ("workspace", ctypes.c_void_p),
         ("seq_offsets", ctypes.c_void_p),
         ("num_seqs", ctypes.c_int64),
+        ("lse", ctypes.c_void_p),
+        ("wait_limit_ns", ctypes.c_uint64),
     ]
 
 

@@ -29,6 +29,10 @@ namespace {
 using chia::MaskGeom;
 
 constexpr uint64_t kDefaultTimeoutNs = 2000000000ull;  // 2 s per barrier wait
+// Waits for a CTA's own copies and MMAs before it exits keep this limit
+// whatever params->wait_limit_ns says: a copy lands within microseconds, so
+// the limit only matters when the consumer of a stage aborted first.
+constexpr uint64_t kDrainNs = 2000000000ull;
 
 struct Derived {
   MaskGeom geom;  // in virtual index space
@@ -113,6 +117,7 @@ int validate(const chia_attn_params_t *p) {
   if (!aligned16(p->q) || !aligned16(p->k) || !aligned16(p->v) || !aligned16(p->o))
     return CHIA_ERR_MISALIGNED;
   if ((reinterpret_cast<uintptr_t>(p->workspace) & 15u) != 0) return CHIA_ERR_MISALIGNED;
+  if ((reinterpret_cast<uintptr_t>(p->lse) & 3u) != 0) return CHIA_ERR_MISALIGNED;
   const int64_t *strides[4] = {p->q_stride, p->k_stride, p->v_stride, p->o_stride};
   for (auto *s : strides)
     for (int d = 0; d < 3; ++d) {
@@ -404,7 +409,9 @@ int chia_attn_fwd(const chia_attn_params_t *p, void *stream) {
   a.o_sh = p->o_stride[1];
   a.o_ss = p->o_stride[2];
   a.status = p->status;
-  a.timeout_ns = kDefaultTimeoutNs;
+  a.timeout_ns = p->wait_limit_ns > 0 ? p->wait_limit_ns : kDefaultTimeoutNs;
+  a.drain_ns = kDrainNs;
+  a.lse = p->norm == CHIA_NORM_SOFTMAX ? p->lse : nullptr;
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int kind = kind_of(p);

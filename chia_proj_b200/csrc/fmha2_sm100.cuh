@@ -164,11 +164,16 @@ __device__ __forceinline__ bool bounded_wait_cl(const WaitCtx &c, uint32_t bar, 
                                                 bool honour_abort = true) {
   if (ptx::mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = ptx::globaltimer_ns();
+  const uint64_t limit = honour_abort ? c.timeout_ns : c.drain_ns;
+  // The clock is read every 64 tries; each try may suspend for up to `hint`
+  // ns, so a short limit also shortens the suspension.
+  const uint32_t hint = limit >= (64ull << 20) ? (1u << 20)
+                                               : static_cast<uint32_t>(limit >> 6) + 32u;
   for (uint32_t it = 1;; ++it) {
-    if (ptx::mbar_try_wait_cluster(bar, parity)) return true;
+    if (ptx::mbar_try_wait_cluster(bar, parity, hint)) return true;
     if ((it & 63u) == 0) {
       if (honour_abort && *c.abort) return false;
-      if (ptx::globaltimer_ns() - t0 > c.timeout_ns) {
+      if (ptx::globaltimer_ns() - t0 > limit) {
         *c.abort = 1;
         if (c.status) atomicOr(c.status, 5 /* CHIA_ERR_DEVICE_TIMEOUT */);
         return false;
@@ -240,6 +245,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
     }
     for (int x = 0; x < 8; ++x) ptx::mbar_init(bar(C::BAR_XCH + x), 2);  // one arrive per warp
     *abort_flag = 0;
+    *reinterpret_cast<volatile int *>(smem + C::OFF_MISC + 24) = -1;
     ptx::fence_barrier_init();
     ptx::fence_proxy_async_smem();
   }
@@ -257,7 +263,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
   ptx::cluster_sync();  // barriers of both CTAs initialised before any remote access
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const WaitCtx wc{abort_flag, args.status, args.timeout_ns};
+  const WaitCtx wc{abort_flag, args.status, args.timeout_ns, args.drain_ns};
+  // unit k of this CTA's last Q-barrier contribution (its Q copy, or the bare
+  // arrival of a keyless unit); -1 = none. The odd CTA hands its value to the
+  // even CTA, which waits for those phases before either CTA exits.
+  int last_q = -1;
+  volatile int *peer_last_q = reinterpret_cast<volatile int *>(smem + C::OFF_MISC + 24);
 
   if (warp == C::LOAD_WARP && lane == 0) {
     // ========== unit scheduler (even CTA) + loads of this CTA's halves ==========
@@ -372,6 +383,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       // this CTA's query tile (zero-filled by TMA when past the sequence end);
       // a unit without key tiles only completes the barrier phase
       const uint32_t qfull = lbar(C::BAR_QFULL + qb);
+      last_q = k;
       if (U.jhi > U.jlo) {
         ptx::mbar_arrive_expect_tx_remote(qfull, C::Q_BYTES);
 #pragma unroll
@@ -397,6 +409,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
     for (int s = 0; s < NKV; ++s)
       if (last_item[s] >= 0)
         bounded_wait(wc, bar(C::BAR_KVEMPTY + s), ((last_item[s] / NKV) & 1), false);
+    if (!leader) ptx::st_shared_cluster_u32(ptx::mapa(sbase + C::OFF_MISC + 24, 0),
+                                            static_cast<uint32_t>(last_q));
   } else if (warp == C::MMA_WARP && leader) {
     // =========================== 2-SM UMMA issuer ===========================
     // The whole warp runs this loop in lockstep; elect.sync inside the
@@ -555,6 +569,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
         // (nothing is staged for the load thread to store).
         if (i < g.sq) {
           const int64_t real_row = static_cast<int64_t>(i) * args.vdil + U.r_res;
+          if (SOFTMAX && args.lse != nullptr && half == 0)
+            store_lse(args, U.b, U.h, real_row, -INFINITY, 0.f);
           uint8_t *orow = reinterpret_cast<uint8_t *>(args.o) +
                           2 * (U.b * args.o_sb + static_cast<int64_t>(U.h) * args.o_sh +
                                real_row * args.o_ss + half * 64);
@@ -682,6 +698,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
         if (!exchange(l_run, l_other)) break;
         const float l_tot = l_run + l_other;
         inv = (l_tot > 0.f) ? 1.0f / l_tot : 0.f;
+        // both halves hold the same running maximum (they agree on every tile's)
+        if (args.lse != nullptr && half == 0 && i < g.sq)
+          store_lse(args, U.b, U.h, static_cast<int64_t>(i) * args.vdil + U.r_res, m_run, l_tot);
       } else if (KIND == KIND_RELU) {
         inv = args.out_scale;
       } else {
@@ -722,6 +741,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
   // ---- teardown: both CTAs finish before TMEM is freed and before either exits ----
   __syncwarp();
   ptx::tc_fence_before();
+  ptx::cluster_sync();
+  // The Q copies of both CTAs complete on the even CTA's q_full barriers.
+  // Unless a wait was abandoned (abort), the MMA warp has already waited for
+  // every phase and the waits below return at once. After an abort they
+  // make sure that no Q copy is still landing when the CTAs exit: the last
+  // phase of each Q buffer either CTA contributed to. A phase whose other
+  // half never came (one CTA stopped first) runs into the drain limit, long
+  // after the one copy of it landed.
+  if (leader && warp == C::LOAD_WARP && lane == 0) {
+    const int kq = last_q > *peer_last_q ? last_q : *peer_last_q;
+    for (int j = kq - 1; j <= kq; ++j)
+      if (j >= 0) bounded_wait(wc, bar(C::BAR_QFULL + (j & 1)), (j >> 1) & 1, false);
+  }
+  __syncwarp();
   ptx::cluster_sync();
   if (warp == C::MMA_WARP) {
     ptx::tc_fence_after();

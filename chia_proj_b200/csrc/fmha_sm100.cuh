@@ -68,7 +68,9 @@ struct KernelArgs {
   void *o;
   int64_t o_sb, o_sh, o_ss;  // output strides (elements)
   int32_t *status;
-  uint64_t timeout_ns;
+  uint64_t timeout_ns;  // limit of every pipeline wait
+  uint64_t drain_ns;    // limit of the waits for this CTA's own copies / MMAs at exit
+  float *lse;           // softmax kinds: natural log-sum-exp per row [B, H, S_q], or null
 };
 
 template <int D>
@@ -138,7 +140,8 @@ struct FmhaConfig {
 struct WaitCtx {
   volatile int *abort;
   int32_t *status;
-  uint64_t timeout_ns;
+  uint64_t timeout_ns;  // pipeline waits
+  uint64_t drain_ns;    // waits that ignore the abort flag (copies and MMAs in flight)
 };
 
 // ------------------------------------------------------------------------
@@ -173,15 +176,23 @@ struct Tracer {
 
 // Bounded wait on an mbarrier phase. Returns false (and raises the CTA abort
 // flag and the device status) when the wait expires or another warp aborted.
+// A wait that ignores the abort flag waits for this CTA's own copies or MMAs
+// before it exits; it keeps its own (long) limit, so that a short pipeline
+// limit never lets a CTA leave with a copy in flight.
 __device__ __forceinline__ bool bounded_wait(const WaitCtx &c, uint32_t bar, uint32_t parity,
                                              bool honour_abort = true) {
   if (ptx::mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = ptx::globaltimer_ns();
+  const uint64_t limit = honour_abort ? c.timeout_ns : c.drain_ns;
+  // The clock is read every 64 tries; each try may suspend for up to `hint`
+  // ns, so a short limit also shortens the suspension.
+  const uint32_t hint = limit >= (64ull << 20) ? (1u << 20)
+                                               : static_cast<uint32_t>(limit >> 6) + 32u;
   for (uint32_t it = 1;; ++it) {
-    if (ptx::mbar_try_wait(bar, parity)) return true;
+    if (ptx::mbar_try_wait(bar, parity, hint)) return true;
     if ((it & 63u) == 0) {
       if (honour_abort && *c.abort) return false;
-      if (ptx::globaltimer_ns() - t0 > c.timeout_ns) {
+      if (ptx::globaltimer_ns() - t0 > limit) {
         *c.abort = 1;
         if (c.status) atomicOr(c.status, 5 /* CHIA_ERR_DEVICE_TIMEOUT */);
         return false;
@@ -450,6 +461,17 @@ __device__ __forceinline__ void store_rows(uint32_t tO, float inv, bool row_ok, 
   }
 }
 
+// Natural log-sum-exp of one row, ln(sum_j e^{s_j}) = (m + log2 l) ln 2, from
+// the running maximum m (log2 domain) and the row sum l = sum 2^(x - m); -inf
+// for a row that sees no key. Layout [B, H, S_q] (real rows), fp32.
+__device__ __forceinline__ void store_lse(const KernelArgs &a, int b, int h, int64_t real_row,
+                                          float m, float l) {
+  constexpr float LN2 = 0.6931471805599453f;
+  const int64_t sq_real = a.mask.sq * a.vdil;
+  const float v = (l > 0.f) ? (m + __log2f(l)) * LN2 : -INFINITY;
+  a.lse[(static_cast<int64_t>(b) * a.heads + h) * sq_real + real_row] = v;
+}
+
 // One work unit: two query tiles (NQ * BM rows) of one (virtual) head.
 struct UnitInfo {
   int r_res, h, b;
@@ -568,7 +590,7 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const WaitCtx wc{abort_flag, args.status, args.timeout_ns};
+  const WaitCtx wc{abort_flag, args.status, args.timeout_ns, args.drain_ns};
 
   if (warp >= 8) {
     ptx::setmaxnreg_dec<C::REG_OTHER>();
@@ -576,6 +598,7 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
       // ==================== scheduler + TMA producer ====================
       Tracer tr(3);
       uint32_t n = 0;  // ring items issued (K and V of every tile)
+      int last_q = -1;  // unit whose Q copies were issued last
       int64_t last_item[NKV];
       for (int s = 0; s < NKV; ++s) last_item[s] = -1;
       auto load_item = [&](const CUtensorMap *map, int64_t j, const UnitInfo &U) -> bool {
@@ -625,6 +648,7 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
         for (int w = 0; w < NQ; ++w)
           if (U.wg_on(w)) qbytes += C::Q_TILE_BYTES;
         ptx::mbar_arrive_expect_tx(bar(C::BAR_Q), qbytes);
+        last_q = k;
 #pragma unroll
         for (int w = 0; w < NQ; ++w)
           if (U.wg_on(w))
@@ -642,11 +666,13 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
         }
         if (!ok) break;
       }
-      // Drain: every copy this thread issued lands before the CTA exits (the
-      // Q copies complete before the MMA thread can finish its last unit).
+      // Drain: every copy this thread issued lands before the CTA exits. The
+      // Q copies of a unit are issued only after the previous unit's have
+      // been consumed, so the last unit's phase is the only one to wait for.
       for (int s = 0; s < NKV; ++s)
         if (last_item[s] >= 0)
           bounded_wait(wc, bar(C::BAR_KVFULL + s), (last_item[s] / NKV) & 1, false);
+      if (last_q >= 0) bounded_wait(wc, bar(C::BAR_Q), last_q & 1, false);
     } else if (warp == C::MMA_WARP) {
       // =========================== UMMA issuer ===========================
       // The whole warp runs this loop in lockstep: readiness is tested by
@@ -844,6 +870,7 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
         // no row of this query tile sees a key: its output is zero
         if (i < g.sq) {
           const int64_t real_row = static_cast<int64_t>(i) * args.vdil + U.r_res;
+          if (SOFTMAX && args.lse != nullptr) store_lse(args, U.b, U.h, real_row, -INFINITY, 0.f);
           uint8_t *orow = reinterpret_cast<uint8_t *>(args.o) +
                           2 * (U.b * args.o_sb + static_cast<int64_t>(U.h) * args.o_sh +
                                real_row * args.o_ss);
@@ -964,6 +991,8 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
                       2 * (U.b * args.o_sb + static_cast<int64_t>(U.h) * args.o_sh +
                            real_row * args.o_ss);
       trs(14);  // O ready
+      if (SOFTMAX && args.lse != nullptr && row_ok)
+        store_lse(args, U.b, U.h, real_row, m_run, l_run);
       store_rows<D, BF16>(tO, inv, row_ok, orow);
       trs(15);  // O stored
       ptx::tc_fence_before();

@@ -70,7 +70,7 @@ _MODS = {"none": N.MOD_NONE, "softcap": N.MOD_SOFTCAP, "alibi": N.MOD_ALIBI,
          "temp": N.MOD_TEMP}
 
 _status_words: Dict[int, torch.Tensor] = {}
-_workspaces: Dict[int, torch.Tensor] = {}
+_workspaces: Dict[tuple, torch.Tensor] = {}
 _param_cache: Dict[tuple, torch.Tensor] = {}
 
 
@@ -83,14 +83,23 @@ def _status_word(device: torch.device) -> torch.Tensor:
     return t
 
 
-def _workspace(device: torch.device) -> torch.Tensor:
-    """Per-device scheduler workspace (zero-filled once; kernels leave it zeroed)."""
+def _workspace(device: torch.device, stream: Optional[int] = None) -> torch.Tensor:
+    """Scheduler workspace of one (device, stream) pair (zero-filled once;
+    every kernel leaves it zeroed).
+
+    Launches on one stream run in order, so they may share a workspace;
+    launches on two streams may overlap on the GPU and would race on the
+    scheduler's counters, so each stream gets its own.
+    """
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    t = _workspaces.get(idx)
+    if stream is None:
+        stream = torch.cuda.current_stream(idx).cuda_stream
+    key = (idx, int(stream))
+    t = _workspaces.get(key)
     if t is None:
         t = torch.zeros(N.WORKSPACE_BYTES // 4, dtype=torch.int32,
                         device=torch.device("cuda", idx))
-        _workspaces[idx] = t
+        _workspaces[key] = t
     return t
 
 
@@ -157,7 +166,7 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
               head_param: Optional[Union[torch.Tensor, Sequence[float]]] = None,
               sig_bias: float = 0.0, out_scale: float = 1.0,
               out: Optional[torch.Tensor] = None, schedule: str = "dynamic",
-              cu_seqlens=None) -> torch.Tensor:
+              cu_seqlens=None, return_lse: bool = False, wait_limit_ns: int = 0):
     """Generic forward attention: ``norm(mask(mod(q.k * scale))) @ v``.
 
     ``q, k, v``: CUDA tensors ``[B, H, S, D]`` (bf16 / fp16; fp32 computed as
@@ -165,14 +174,20 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     ``H % H_kv == 0`` (grouped-query attention: query head ``h`` reads K/V
     head ``h // (H // H_kv)``). ``head_param``: ALiBi slopes (``mod="alibi"``)
     or logit multipliers (``mod="temp"``), one per head. ``schedule``:
-    ``"dynamic"`` balances work units over the SMs with a per-device
-    workspace; ``"static"`` assigns them round-robin and uses no workspace.
+    ``"dynamic"`` balances work units over the SMs with a workspace per
+    (device, stream); ``"static"`` assigns them round-robin and uses none.
     ``cu_seqlens``: packed variable-length sequences. ``q, k, v`` hold a
     batch of 1 whose ``S`` tokens are the concatenated sequences, with
     sequence ``s`` at tokens ``[cu_seqlens[s], cu_seqlens[s+1])``; a query
     sees keys of its own sequence only (then ``mask``, which may not use a
     block, prefix or dilation). A list or CPU tensor is checked and copied to
     the device; a CUDA int32 tensor is used as given.
+    ``return_lse``: also return the natural log-sum-exp of every row's
+    modified, masked scores, fp32 ``[B, H, S]`` (softmax only; ``-inf`` for a
+    row that sees no key) -- what the backward pass needs.
+    ``wait_limit_ns``: limit of each in-kernel wait (0 = 2 s). A wait that
+    runs out is reported by ``check_device_status``; tests use tiny values to
+    exercise that path.
     """
     if schedule not in ("dynamic", "static"):
         raise ValueError(f"unknown schedule {schedule!r}")
@@ -196,6 +211,10 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     if D not in (64, 128):
         raise ValueError(f"head_dim {D} unsupported (64 or 128)")
     mask = mask.validate()
+    if return_lse and norm != "softmax":
+        raise ValueError("return_lse needs norm='softmax'")
+    if wait_limit_ns < 0:
+        raise ValueError("wait_limit_ns must be >= 0")
     in_dtype = q.dtype
     if in_dtype == torch.float32:
         q, k, v = q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16)
@@ -258,16 +277,21 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     if seg is not None:
         p.seq_offsets = seg.data_ptr()
         p.num_seqs = seg.numel() - 1
-    # One workspace per device: calls on different streams of one device would
-    # race on it, so only the current stream of the device is used here.
-    p.workspace = _workspace(dev).data_ptr() if schedule == "dynamic" else None
+    lse = None
+    if return_lse:
+        lse = torch.empty(B, H, S, dtype=torch.float32, device=dev)
+        p.lse = lse.data_ptr()
+    p.wait_limit_ns = int(wait_limit_ns)
 
     lib = N.load()
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev).cuda_stream
+        # one workspace per (device, stream): see _workspace
+        p.workspace = _workspace(dev, stream).data_ptr() if schedule == "dynamic" else None
         N.check(lib.chia_attn_fwd(ctypes.byref(p), ctypes.c_void_p(stream)),
                 f"chia_attn_fwd(norm={norm}, mod={mod}, mask={mask}, shape={tuple(q.shape)})")
-    return o.float() if in_dtype == torch.float32 else o
+    o = o.float() if in_dtype == torch.float32 else o
+    return (o, lse) if return_lse else o
 
 
 # ---------------------------------------------------------------------------

@@ -56,7 +56,7 @@ extern "C" {
 #define CHIA_API
 #endif
 
-#define CHIA_ATTN_ABI_VERSION 3
+#define CHIA_ATTN_ABI_VERSION 4
 
 /* Size of the optional scheduler workspace (bytes). */
 #define CHIA_ATTN_WORKSPACE_BYTES 256
@@ -151,6 +151,21 @@ typedef struct chia_attn_params {
    * reference, whose operators take one fixed length per batch. */
   const int32_t *seq_offsets;
   int64_t num_seqs;
+
+  /* Optional device fp32 [batch, heads, seqlen_q] (contiguous, 4-byte
+   * aligned): for CHIA_NORM_SOFTMAX the natural log-sum-exp of each row's
+   * modified, masked scores, ln sum_j exp(s_ij) (-inf for a row that sees no
+   * key); the backward pass reads it. Ignored for the sigmoid and ReLU
+   * normalisers. NULL = not written. The reference's eager functions do not
+   * return it. */
+  float *lse;
+
+  /* Limit of each in-kernel wait, in nanoseconds; 0 = the default (2 s). A
+   * wait that runs out ORs CHIA_ERR_DEVICE_TIMEOUT into *status and the
+   * kernel returns early, with its outputs unspecified; waits for the
+   * kernel's own copies and MMAs before it exits keep the default limit.
+   * Small values exist so that a test can make a wait run out. */
+  uint64_t wait_limit_ns;
 } chia_attn_params_t;
 
 /* Forward attention on `stream` (cudaStream_t; NULL = legacy default

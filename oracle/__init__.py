@@ -22,6 +22,7 @@ from .eager import (  # noqa: F401
     OPS,
     reference_masks,
     run_op,
+    run_op_lse,
     run_varlen,
     visible_pairs_dense,
 )

@@ -32,7 +32,11 @@ from typing import Callable, Dict, Optional
 import torch
 import torch.nn.functional as F
 
-__all__ = ["OPS", "run_op", "reference_masks", "visible_pairs_dense"]
+__all__ = ["OPS", "run_op", "run_op_lse", "reference_masks", "visible_pairs_dense"]
+
+# When set (by run_op_lse), _eval stores each softmax row's natural
+# log-sum-exp of the modified, masked scores here, [B, H, S_q].
+_lse_sink: Optional[torch.Tensor] = None
 
 
 # ---------------------------------------------------------------------------
@@ -115,7 +119,10 @@ def _eval(q, k, v, *, maskfn, norm="softmax", mod=None, scale=None,
                     s = mod(s, h, i, j)
                 ok = maskfn(i, j)
                 if norm == "softmax":
-                    p = torch.softmax(s.masked_fill(~ok, float("-inf")), -1)
+                    sm = s.masked_fill(~ok, float("-inf"))
+                    p = torch.softmax(sm, -1)
+                    if _lse_sink is not None:
+                        _lse_sink[b, h, i0:i1] = torch.logsumexp(sm, -1).detach()
                 elif norm == "sigmoid":
                     p = torch.sigmoid(s) * ok.float()
                 elif norm == "relu":
@@ -224,6 +231,22 @@ OPS = {
 def run_op(op: str, q, k, v, **params) -> torch.Tensor:
     """Run reference operator ``op`` in fp32 on CPU; returns fp32 ``[B,H,S,D]``."""
     return OPS[op](q.cpu(), k.cpu(), v.cpu(), **params)
+
+
+def run_op_lse(op: str, q, k, v, **params):
+    """``run_op`` plus the natural log-sum-exp of every softmax row's
+    modified, masked scores (``-inf`` where a row sees no key), fp32
+    ``[B, H, S_q]``. Not part of the reference, whose eager functions return
+    the output only; it pins the forward's LSE output, which the backward
+    pass reads."""
+    global _lse_sink
+    B, H, Sq, _ = q.shape
+    _lse_sink = torch.full((B, H, Sq), float("-inf"))
+    try:
+        out = run_op(op, q, k, v, **params)
+        return out, _lse_sink
+    finally:
+        _lse_sink = None
 
 
 def run_varlen(op: str, q, k, v, cu_seqlens, **params) -> torch.Tensor:

@@ -97,6 +97,7 @@ def _valid_params():
     (lambda p: setattr(p, "scale", float("nan")), 1),
     (lambda p: setattr(p, "heads_kv", 3), 1),    # 4 query heads, 3 K/V heads
     (lambda p: setattr(p, "heads_kv", -1), 1),
+    (lambda p: setattr(p, "lse", 0x30002), 3),   # log-sum-exp output not 4-byte aligned
     # packed sequences: batch must be 1 ...
     (lambda p: (setattr(p, "seq_offsets", 0x20000), setattr(p, "num_seqs", 2)), 1),
     # ... a prefix (or block, dilation) is not supported with them ...

@@ -37,6 +37,8 @@ def _worker(rank, ws, port, units, q):
         t_ms = 10.0 + rank  # a per-rank time: the job time is the slowest rank
         t_max = bench.max_over_ranks(t_ms, torch.device("cpu"), ws)
         errs = bench.gather_max([0.001 * (rank + 1), 0.5 - 0.1 * rank], torch.device("cpu"), ws)
+        per_rank = bench.gather_all([1000.0 + rank, 2.0 * rank], torch.device("cpu"), ws)
+        assert per_rank == [[1000.0 + r, 2.0 * r] for r in range(ws)]
         q.put((rank, env, lo, hi, local, t_max, errs))
     finally:
         dist.destroy_process_group()
@@ -73,3 +75,15 @@ def test_single_rank_needs_no_process_group():
     assert bench.shard(1024, 1, 0) == (0, 1024)
     assert bench.max_over_ranks(3.5, torch.device("cpu"), 1) == 3.5
     assert bench.gather_max([1.0, 2.0], torch.device("cpu"), 1) == [1.0, 2.0]
+    assert bench.gather_all([1.0, 2.0], torch.device("cpu"), 1) == [[1.0, 2.0]]
+
+
+def test_per_head_parameters_follow_the_shard():
+    """The headline suite flattens (batch, head) into units u = b*H + h and
+    shards them; unit u must carry head u % H's parameter."""
+    H = 16
+    vals = torch.arange(H, dtype=torch.float32) * 10
+    for ws in (1, 2, 4, 8):
+        got = torch.cat([bench._flat_param(vals, *bench.shard(4 * H, ws, r), H)
+                         for r in range(ws)])
+        assert torch.equal(got, vals.repeat(4))

@@ -182,6 +182,12 @@ def test_linearity_in_v_is_exact(cuda):
     ("bias_sliding_window", {}), ("bias_block_diagonal", dict(block=256)),
     ("bias_prefix_lm", dict(prefix=1024)), ("bias_dilated", {}), ("softcap_gemma2", {}),
     ("bias_local", {}),
+    # the causal kinds the headline suite times
+    ("bias_alibi", dict(slopes=cp.alibi_slopes_geometric(16))),
+    ("temp_perhead", dict(temps=1.0 / _tau(16))),
+    ("softcap_gemma2", dict(cap=50.0)),
+    ("sigmoid_attn", {}),
+    ("relu_attn", dict(out_scale=1.0 / 4096)),
 ])
 def test_invisible_keys_do_not_matter_at_headline_shape(cuda, op, kw):
     """B4 H16 S4096 D128: perturbing keys/values a mask hides leaves the output
@@ -211,9 +217,79 @@ def test_invisible_keys_do_not_matter_at_headline_shape(cuda, op, kw):
     out2 = cp.OPS[op](q, k2, v2, **kw)
     assert torch.equal(out[:, :, 3000:3100], out2[:, :, 3000:3100])
     for (b, h) in ((0, 0), (3, 15)):
+        # per-head parameters follow the sliced head
+        okw = {n: (x[h:h + 1] if n in ("slopes", "temps") else x) for n, x in kw.items()}
         ref = oracle.run_op(op, q[b:b + 1, h:h + 1].cpu(), k[b:b + 1, h:h + 1].cpu(),
-                            v[b:b + 1, h:h + 1].cpu(), **kw)
+                            v[b:b + 1, h:h + 1].cpu(), **okw)
         check(out[b:b + 1, h:h + 1], ref, f"{op} head ({b},{h})")
+
+
+@pytest.mark.parametrize("op", ["bias_alibi", "temp_perhead"])
+def test_config3_at_its_own_shape(cuda, op):
+    """BASELINE config 3 exactly as the bench times it: B8 H32 S4096 D128 fp16,
+    causal; ALiBi slopes 2^(-8(h+1)/H), temperatures 1/tau_h with
+    tau_h ~ U[0.5, 2] from seed 0. Three sampled heads against the oracle,
+    among them the last head (smallest slope, 2^-8)."""
+    B, H, S, D = 8, 32, 4096, 128
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(3)
+    q, k, v = (torch.randn(B, H, S, D, generator=g, device=dev).to(torch.float16)
+               for _ in range(3))
+    if op == "bias_alibi":
+        kw = dict(slopes=cp.alibi_slopes_geometric(H))
+    else:
+        kw = dict(temps=1.0 / _tau(H))
+    out = cp.OPS[op](q, k, v, **kw)
+    torch.cuda.synchronize()
+    for (b, h) in ((0, 0), (3, 17), (7, 31)):
+        sl = lambda x: x[b:b + 1, h:h + 1].cpu()
+        okw = dict(slopes=kw["slopes"][h:h + 1]) if op == "bias_alibi" else \
+            dict(temps=kw["temps"][h:h + 1])
+        ref = oracle.run_op(op, sl(q), sl(k), sl(v), **okw)
+        check(out[b:b + 1, h:h + 1], ref, f"{op} config 3 head ({b},{h})")
+
+
+def test_config2_every_head(cuda):
+    """BASELINE config 2 in full: causal sliding window 256, B4 H16 S2048
+    D64 bf16, all 64 heads against the oracle."""
+    q, k, v = gen(4, 16, 2048, 64, torch.bfloat16, seed=2)
+    ref = oracle.run_op("bias_sliding_window", q, k, v, window=256)
+    check(run("bias_sliding_window", q, k, v, window=256), ref, "config 2")
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("op,kw", [("softcap_gemma2", {}), ("bias_sliding_window", {}),
+                                   ("bias_alibi", {}), ("bias_dilated", {}),
+                                   ("bias_prefix_lm", dict(prefix=300)),
+                                   ("softcap_gemma2", dict(cap=50.0, causal=False))])
+def test_log_sum_exp_output(cuda, op, kw, D):
+    """The per-row log-sum-exp the forward writes for the backward pass,
+    against the oracle's, on a ragged length."""
+    q, k, v = gen(2, 3, 1000, D, torch.bfloat16, seed=D + 5)
+    ref_o, ref_lse = oracle.run_op_lse(op, q, k, v, **kw)
+    dev = torch.device("cuda", 0)
+    mask = cp.op_config(op, **kw)
+    mod = {"softcap_gemma2": "softcap", "bias_alibi": "alibi"}.get(op, "none")
+    extra = dict(softcap=kw.get("cap", 30.0)) if mod == "softcap" else {}
+    o, lse = cp.attention(q.to(dev), k.to(dev), v.to(dev), mod=mod, mask=mask,
+                          return_lse=True, **extra)
+    torch.cuda.synchronize()
+    check(o, ref_o, f"{op} D={D}")
+    err = (lse.cpu() - ref_lse).abs().max().item()
+    assert err < 1e-3, f"{op} D={D}: lse max error {err}"
+
+
+def test_log_sum_exp_of_rows_without_keys(cuda):
+    """Rows that see no key (S_q > S_kv with a window) get -inf."""
+    dev = torch.device("cuda", 0)
+    q, _, _ = gen(1, 2, 600, 128, torch.bfloat16, seed=83)
+    _, k, v = gen(1, 2, 128, 128, torch.bfloat16, seed=84)
+    o, lse = cp.attention(q.to(dev), k.to(dev), v.to(dev), mask=cp.Mask(left=63, right=0),
+                          return_lse=True)
+    torch.cuda.synchronize()
+    lse = lse.cpu()
+    assert torch.isinf(lse[:, :, 191:]).all() and (lse[:, :, 191:] < 0).all()
+    assert torch.isfinite(lse[:, :, :191]).all()
 
 
 @pytest.mark.parametrize("op", ["sigmoid_attn", "relu_attn"])
@@ -407,3 +483,66 @@ def test_keyless_units_write_zeros(cuda, norm, D):
         assert (got[:, :, Skv + W - 1:] == 0).all(), "keyless rows must be zero"
         check(out, ref, f"{norm} D={D} {schedule}")
         out.fill_(7.0)
+
+
+# ------------------------------------------ two streams, dynamic schedule
+def test_concurrent_streams_do_not_share_a_scheduler(cuda):
+    """Launches on two streams of one device may overlap on the GPU; each
+    stream has its own scheduler workspace, so every unit still runs exactly
+    once: outputs equal the static schedule's, bit for bit, and every
+    workspace is left zeroed."""
+    from chia_proj_b200 import ops
+    dev = torch.device("cuda", 0)
+    inputs = [tuple(t.to(dev) for t in gen(4, 16, 2048, D, torch.bfloat16, seed=90 + D))
+              for D in (128, 64)]
+    want = [cp.softcap_gemma2(*x, cap=50.0) for x in inputs]
+    want_static = [cp.attention(*x, mod="softcap", softcap=50.0, schedule="static")
+                   for x in inputs]
+    for a, b in zip(want, want_static):
+        assert torch.equal(a, b)
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(dev), torch.cuda.Stream(dev)]
+    got = [[], []]
+    for rep in range(6):
+        for si, st in enumerate(streams):
+            with torch.cuda.stream(st):
+                x = inputs[(rep + si) % 2]
+                for t in x:
+                    t.record_stream(st)
+                got[si].append(((rep + si) % 2, cp.softcap_gemma2(*x, cap=50.0)))
+    torch.cuda.synchronize()
+    for lst in got:
+        for which, o in lst:
+            assert torch.equal(o, want[which])
+    for st in streams:
+        assert int(ops._workspace(dev, st.cuda_stream).abs().sum()) == 0
+
+
+# ------------------------------------------------ a bounded wait that runs out
+@pytest.mark.parametrize("D", [128, 64])
+def test_wait_that_runs_out_is_reported_and_the_device_recovers(cuda, D):
+    """With a wait limit of a few nanoseconds the first wait that is not met
+    at once runs out: the kernel sets CHIA_ERR_DEVICE_TIMEOUT in the status
+    word, drains its own copies and MMAs, frees its tensor memory and
+    returns (no trap, no hang). check_device_status() raises it, and the next
+    call with the default limit on the same device is correct and leaves the
+    scheduler workspace zeroed."""
+    from chia_proj_b200 import ops
+    dev = torch.device("cuda", 0)
+    q, k, v = gen(2, 4, 2048, D, torch.bfloat16, seed=95)
+    qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+    cp.check_device_status(0)
+    code = 0
+    for _ in range(3):   # a wait that happens to be met at once every time would not run out
+        cp.attention(qd, kd, vd, mod="softcap", wait_limit_ns=1)
+        torch.cuda.synchronize()
+        try:
+            cp.check_device_status(0)
+        except cp.ChiaError as e:
+            code = e.code
+            break
+    assert code == 5, "no wait ran out"
+    torch.cuda.synchronize()
+    assert int(ops._workspace(dev).abs().sum()) == 0
+    check(cp.softcap_gemma2(qd, kd, vd), oracle.run_op("softcap_gemma2", q, k, v),
+          "after a timeout")
