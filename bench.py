@@ -239,13 +239,16 @@ def _flat_param(values: torch.Tensor, lo: int, hi: int, H: int) -> torch.Tensor:
     return values[torch.arange(lo, hi) % H]
 
 
-def headline_suite(device, rank: int = 0, ws: int = 1):
+def headline_suite(device, rank: int = 0, ws: int = 1, profile_launches: bool = False):
     """All ten operators at the north-star shape B4 H16 S4096 D128 (+ configs
     1-3 at N=1). The B*H units are split over the ranks like config 5 (each
     rank runs its contiguous range of (batch, head) units, per-head
     parameters follow their head); a variant's time is the maximum over ranks
     of its CUDA-event time. Inputs that fit in L2 rotate over enough copies
-    that every launch reads from HBM."""
+    that every launch reads from HBM.
+
+    ``profile_launches``: launch each headline variant and config 2 exactly
+    once, untimed, in the suite's order (for one ncu capture per variant)."""
     import chia_proj_b200 as cp
     pk, src = peaks()
     p_tensor = pk.get("bf16_tflops", FALLBACK["bf16_tflops"])
@@ -260,6 +263,10 @@ def headline_suite(device, rank: int = 0, ws: int = 1):
                       for _ in range(3)) for _ in range(n)]
 
     def bench_one(fn, sets, mask, units_total, Sx, Dx, iters=10, profile=None):
+        if profile_launches:
+            fn(*sets[0])
+            torch.cuda.synchronize()
+            return {"launched": 1}
         for i in range(3):
             fn(*sets[i % len(sets)])
         torch.cuda.synchronize()
@@ -330,6 +337,12 @@ def headline_suite(device, rank: int = 0, ws: int = 1):
     del sets
     if ws > 1:
         torch.cuda.empty_cache()
+        return out
+    if profile_launches:
+        B2, H2, S2, D2 = 4, 16, 2048, 64
+        sets = make_sets(B2 * H2, S2, D2, torch.bfloat16, 11)
+        out["config2"] = bench_one(cp.bias_sliding_window, sets[:1],
+                                   cp.op_config("bias_sliding_window"), B2 * H2, S2, D2)
         return out
     with ClockSampler(torch.cuda.current_device()) as clk:
         # config 2: causal window 256, D=64 (67 MB: rotated over 8 input sets)
@@ -665,6 +678,8 @@ def main(argv=None):
                     help="(batch, head) units per host<->device chunk in the e2e measurement")
     ap.add_argument("--suite-only", action="store_true",
                     help="run only the per-variant suite at the north-star shape (1 GPU)")
+    ap.add_argument("--profile-launches", action="store_true",
+                    help="launch each headline variant and config 2 once, untimed (ncu)")
     ap.add_argument("--units", type=int, default=B_TOTAL * H_TOTAL,
                     help="(batch, head) units in the job; smaller values are for ncu captures")
     a = ap.parse_args(argv)
@@ -672,9 +687,11 @@ def main(argv=None):
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if a.impl == "reference":
         run_reference(a)
-    elif a.suite_only:
+    elif a.suite_only or a.profile_launches:
         torch.cuda.set_device(0)
-        print(json.dumps({"suite": headline_suite(torch.device("cuda", 0))}), flush=True)
+        print(json.dumps({"suite": headline_suite(torch.device("cuda", 0),
+                                                  profile_launches=a.profile_launches)}),
+              flush=True)
     else:
         run_ours(a)
 

@@ -165,13 +165,15 @@ __device__ __forceinline__ bool bounded_wait_cl(const WaitCtx &c, uint32_t bar, 
   if (ptx::mbar_try_wait_cluster(bar, parity)) return true;
   const uint64_t t0 = ptx::globaltimer_ns();
   const uint64_t limit = honour_abort ? c.timeout_ns : c.drain_ns;
-  // The clock is read every 64 tries; each try may suspend for up to `hint`
-  // ns, so a short limit also shortens the suspension.
-  const uint32_t hint = limit >= (64ull << 20) ? (1u << 20)
-                                               : static_cast<uint32_t>(limit >> 6) + 32u;
+  // Each try may suspend for up to `hint` ns. With the default limit the
+  // clock is read every 64 tries; a short limit (tests) shortens the
+  // suspension and reads the clock after every try.
+  const bool short_limit = limit < (64ull << 20);
+  const uint32_t hint = short_limit ? static_cast<uint32_t>(limit >> 6) + 32u : (1u << 20);
+  const uint32_t check_mask = short_limit ? 0u : 63u;
   for (uint32_t it = 1;; ++it) {
     if (ptx::mbar_try_wait_cluster(bar, parity, hint)) return true;
-    if ((it & 63u) == 0) {
+    if ((it & check_mask) == 0) {
       if (honour_abort && *c.abort) return false;
       if (ptx::globaltimer_ns() - t0 > limit) {
         *c.abort = 1;
