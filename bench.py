@@ -377,9 +377,49 @@ def headline_suite(device, rank: int = 0, ws: int = 1, profile_launches: bool = 
         out["config1"] = {"shape": {"B": 1, "H": 8, "S": 512, "D": 64, "dtype": "fp32"},
                           "softcap_gemma2": c1}
         del sets
+        out["decode"] = decode_bench(device)
     out["configs_clocks"] = clk.summary()
     torch.cuda.empty_cache()
     return out
+
+
+def decode_bench(device, iters: int = 20):
+    """Decode step of a grouped-query model: one new query per sequence over
+    8192 cached keys, B8, 32 query heads on 4 K/V heads, D128 bf16, causal
+    (every cached key visible). HBM-bound: the bytes are K and V, read once.
+    Timed on the split-KV decode kernel and, for comparison, on the tiled
+    kernel (split_kv=False); three input sets rotate (134 MB each)."""
+    import chia_proj_b200 as cp
+    B, H, Hkv, Skv, D_ = 8, 32, 4, 8192, 128
+    g = torch.Generator(device=device).manual_seed(5)
+    sets = [(torch.randn(B, H, 1, D_, generator=g, device=device).to(torch.bfloat16),
+             torch.randn(B, Hkv, Skv, D_, generator=g, device=device).to(torch.bfloat16),
+             torch.randn(B, Hkv, Skv, D_, generator=g, device=device).to(torch.bfloat16))
+            for _ in range(3)]
+    mask = cp.Mask(left=-1, right=Skv - 1)
+    pk, _ = peaks()
+    hbm = pk.get("hbm_gbs", FALLBACK["hbm_gbs"])
+    res = {"shape": {"B": B, "H": H, "H_kv": Hkv, "S_q": 1, "S_kv": Skv, "D": D_,
+                     "dtype": "bf16"}}
+    by = 2 * B * Hkv * Skv * D_ * 2 + 2 * B * H * D_ * 2
+    fl = 4 * D_ * Skv * B * H
+    for name, split in (("split_kv", True), ("tiled", False)):
+        fn = lambda q, k, v: cp.attention(q, k, v, mask=mask, split_kv=split)
+        for i in range(3):
+            fn(*sets[i % 3])
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        for i in range(iters):
+            fn(*sets[i % 3])
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        res[name] = {"us": round(ms * 1e3, 1), "hbm_gbs": round(by / ms / 1e6, 1),
+                     "frac_hbm": round(by / ms / 1e6 / hbm, 3),
+                     "tflops": round(fl / ms / 1e9, 2)}
+    del sets
+    return res
 
 
 def preheat(step, seconds: float):

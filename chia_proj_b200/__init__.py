@@ -32,3 +32,4 @@ from .ops import (  # noqa: F401
     visible_pairs,
 )
 from ._native import ChiaError  # noqa: F401
+from . import flex  # noqa: F401,E402

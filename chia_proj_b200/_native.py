@@ -40,6 +40,8 @@ EXPORTED_SYMBOLS = (
     "chia_attn_tile_plan",
     "chia_attn_status_string",
     "chia_attn_abi_version",
+    "chia_attn_decode",
+    "chia_attn_decode_workspace_bytes",
 )
 
 
@@ -113,6 +115,11 @@ def load() -> ctypes.CDLL:
             lib.chia_attn_fwd.restype = ctypes.c_int
             lib.chia_attn_fwd_noalloc.argtypes = [ctypes.POINTER(AttnParams), ctypes.c_void_p]
             lib.chia_attn_fwd_noalloc.restype = ctypes.c_int
+            lib.chia_attn_decode.argtypes = [ctypes.POINTER(AttnParams), ctypes.c_void_p,
+                                             ctypes.c_int64, ctypes.c_void_p]
+            lib.chia_attn_decode.restype = ctypes.c_int
+            lib.chia_attn_decode_workspace_bytes.argtypes = [ctypes.POINTER(AttnParams)]
+            lib.chia_attn_decode_workspace_bytes.restype = ctypes.c_int64
             lib.chia_attn_visible_pairs.argtypes = [ctypes.POINTER(AttnParams)]
             lib.chia_attn_visible_pairs.restype = ctypes.c_int64
             lib.chia_attn_tile_plan.argtypes = [

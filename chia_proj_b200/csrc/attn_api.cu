@@ -22,6 +22,7 @@
 #include <mutex>
 
 #include "../../include/chia_attn.h"
+#include "decode_sm100.cuh"
 #include "fmha2_sm100.cuh"
 
 namespace {
@@ -300,9 +301,163 @@ int noalloc_scratch_addr(int dev, void **out) {
   return CHIA_OK;
 }
 
+// ------------------------------------------------------- split-KV decode
+// Plan of a decode-shaped call: rows per K/V head, their padding, the key
+// range all rows can see, and how it is split over CTAs.
+struct DecodePlan {
+  int rows, rp;
+  int64_t nkvh;
+  int64_t key_lo, nkeys;
+  int32_t kps, splits;
+  int64_t off_tickets, off_o, off_ml, bytes;  // workspace layout
+};
+
+constexpr int kDecodeMaxRows = 32;
+constexpr int64_t kDecodeMaxHeads = 65535;  // batch * K/V heads (grid y)
+
+int decode_plan(const chia_attn_params_t *p, int sms, DecodePlan &pl) {
+  if (p->seq_offsets != nullptr) return CHIA_ERR_UNSUPPORTED;
+  const int64_t hkv = p->heads_kv > 0 ? p->heads_kv : p->heads;
+  const int64_t group = p->heads / hkv;
+  if (group * p->seqlen_q > kDecodeMaxRows) return CHIA_ERR_UNSUPPORTED;
+  pl.rows = static_cast<int>(group * p->seqlen_q);
+  pl.rp = pl.rows <= 16 ? 16 : 32;  // MMA row tiles of 16
+  pl.nkvh = p->batch * hkv;
+  // key hull of rows [0, S_q): lo() and hi() do not decrease with the row
+  const MaskGeom g = real_geom(p);
+  int64_t lo0, hi0, lo1, hi1;
+  chia::row_band(g, 0, lo0, hi0);
+  chia::row_band(g, p->seqlen_q - 1, lo1, hi1);
+  int64_t klo = lo0, khi = hi1;
+  if (g.prefix > 0) {
+    klo = 0;
+    khi = khi > g.prefix - 1 ? khi : g.prefix - 1;
+  }
+  pl.key_lo = klo;
+  pl.nkeys = khi >= klo ? khi - klo + 1 : 0;
+  constexpr int TK = 64;
+  const int64_t min_keys = 4 * TK;  // per split: amortises the Q load and the merge
+  int64_t splits = (4 * static_cast<int64_t>(sms) + pl.nkvh - 1) / pl.nkvh;
+  const int64_t by_keys = (pl.nkeys + min_keys - 1) / min_keys;
+  if (splits > by_keys) splits = by_keys;
+  if (splits < 1) splits = 1;
+  int64_t kps = (pl.nkeys + splits - 1) / splits;
+  kps = (kps + TK - 1) / TK * TK;
+  if (kps < TK) kps = TK;
+  splits = pl.nkeys > 0 ? (pl.nkeys + kps - 1) / kps : 1;
+  if (kps > 0x7fffffff || splits > 0xffff) return CHIA_ERR_UNSUPPORTED;
+  pl.kps = static_cast<int32_t>(kps);
+  pl.splits = static_cast<int32_t>(splits);
+  // Workspace: the tickets first, at a fixed place and size (one per possible
+  // (batch, K/V head) -- the grid's y limit), so that they stay zero whatever
+  // the plans of earlier calls were; then the splits' partial results, which
+  // every call overwrites.
+  if (pl.nkvh > kDecodeMaxHeads) return CHIA_ERR_UNSUPPORTED;
+  auto up256 = [](int64_t x) { return (x + 255) / 256 * 256; };
+  const int64_t n_part = pl.nkvh * splits * pl.rp;
+  pl.off_tickets = 0;
+  pl.off_o = up256(kDecodeMaxHeads * 4);  // 256-byte aligned, like every region
+  pl.off_ml = pl.off_o + up256(n_part * p->head_dim * 4);
+  pl.bytes = pl.off_ml + up256(n_part * 2 * 4);
+  // the merge reads the partial outputs as 8-byte pairs
+  if ((pl.off_o | pl.off_ml) & 255) return CHIA_ERR_LAUNCH;
+  return CHIA_OK;
+}
+
+template <int D, int RP, bool BF16>
+int launch_decode(const chia::DecodeArgs &a, dim3 grid, cudaStream_t s) {
+  auto kern = chia::decode_kernel<D, RP, BF16>;
+  constexpr int smem = chia::decode_smem_bytes<D, RP>();
+  static std::atomic<uint32_t> configured{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHIA_ERR_NO_DEVICE;
+  const uint32_t bit = 1u << (dev & 31);
+  if (!(configured.load(std::memory_order_acquire) & bit)) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return CHIA_ERR_LAUNCH;
+    configured.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  kern<<<grid, 128, smem, s>>>(a);
+  return cudaGetLastError() == cudaSuccess ? CHIA_OK : CHIA_ERR_LAUNCH;
+}
+
+template <int D, bool BF16>
+int launch_decode_rp(int rp, const chia::DecodeArgs &a, dim3 grid, cudaStream_t s) {
+  return rp == 16 ? launch_decode<D, 16, BF16>(a, grid, s) : launch_decode<D, 32, BF16>(a, grid, s);
+}
+
 }  // namespace
 
 extern "C" {
+
+int64_t chia_attn_decode_workspace_bytes(const chia_attn_params_t *p) {
+  if (validate(p) != CHIA_OK) return -1;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
+    sms = 148;  // host-only callers (no GPU): size for a B200
+  DecodePlan pl;
+  if (decode_plan(p, sms, pl) != CHIA_OK) return -1;
+  return pl.bytes;
+}
+
+int chia_attn_decode(const chia_attn_params_t *p, void *workspace, int64_t workspace_bytes,
+                     void *stream) {
+  const int v = validate(p);
+  if (v != CHIA_OK) return v;
+  int dev = 0, major = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHIA_ERR_NO_DEVICE;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      major != 10)
+    return CHIA_ERR_NO_DEVICE;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
+    return CHIA_ERR_NO_DEVICE;
+  DecodePlan pl;
+  const int r = decode_plan(p, sms, pl);
+  if (r != CHIA_OK) return r;
+  if (workspace == nullptr || workspace_bytes < pl.bytes) return CHIA_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return CHIA_ERR_MISALIGNED;
+  chia::DecodeArgs a{};
+  a.q = p->q;
+  a.k = p->k;
+  a.v = p->v;
+  a.o = p->o;
+  a.q_sb = p->q_stride[0]; a.q_sh = p->q_stride[1]; a.q_ss = p->q_stride[2];
+  a.k_sb = p->k_stride[0]; a.k_sh = p->k_stride[1]; a.k_ss = p->k_stride[2];
+  a.v_sb = p->v_stride[0]; a.v_sh = p->v_stride[1]; a.v_ss = p->v_stride[2];
+  a.o_sb = p->o_stride[0]; a.o_sh = p->o_stride[1]; a.o_ss = p->o_stride[2];
+  const int64_t hkv = p->heads_kv > 0 ? p->heads_kv : p->heads;
+  a.heads = static_cast<int32_t>(p->heads);
+  a.heads_kv = static_cast<int32_t>(hkv);
+  a.group = static_cast<int32_t>(p->heads / hkv);
+  a.sq = static_cast<int32_t>(p->seqlen_q);
+  a.rows = pl.rows;
+  a.kind = kind_of(p);
+  a.mask = real_geom(p);
+  a.key_lo = pl.key_lo;
+  a.keys_per_split = pl.kps;
+  a.splits = pl.splits;
+  a.score_scale = p->scale;
+  a.softcap = p->softcap;
+  a.sig_bias = p->sig_bias;
+  a.out_scale = p->out_scale;
+  a.head_param = (p->mod == CHIA_MOD_ALIBI || p->mod == CHIA_MOD_TEMP) ? p->head_param : nullptr;
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  a.tickets = reinterpret_cast<int32_t *>(ws + pl.off_tickets);
+  a.part_o = reinterpret_cast<float *>(ws + pl.off_o);
+  a.part_ml = reinterpret_cast<float *>(ws + pl.off_ml);
+  a.lse = p->norm == CHIA_NORM_SOFTMAX ? p->lse : nullptr;
+  const dim3 grid(static_cast<unsigned>(pl.splits), static_cast<unsigned>(pl.nkvh));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool bf16 = p->dtype == CHIA_DTYPE_BF16;
+  if (p->head_dim == 128)
+    return bf16 ? launch_decode_rp<128, true>(pl.rp, a, grid, s)
+                : launch_decode_rp<128, false>(pl.rp, a, grid, s);
+  return bf16 ? launch_decode_rp<64, true>(pl.rp, a, grid, s)
+              : launch_decode_rp<64, false>(pl.rp, a, grid, s);
+}
+
 
 int chia_attn_abi_version(void) { return CHIA_ATTN_ABI_VERSION; }
 

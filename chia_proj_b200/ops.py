@@ -103,6 +103,23 @@ def _workspace(device: torch.device, stream: Optional[int] = None) -> torch.Tens
     return t
 
 
+_decode_workspaces: Dict[tuple, torch.Tensor] = {}
+
+
+def _decode_workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    """Workspace of the split-KV decode path for one (device, stream): zero-
+    filled when (re)allocated, left with zeroed counters by every call."""
+    key = (device.index, int(stream))
+    t = _decode_workspaces.get(key)
+    if t is None or t.numel() < nbytes:
+        t = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+        _decode_workspaces[key] = t
+    return t
+
+
+DECODE_MAX_ROWS = 32  # (H / H_kv) * S_q of a decode-shaped call
+
+
 def check_device_status(device: Optional[Union[int, torch.device]] = None) -> None:
     """Synchronise ``device`` and raise if any kernel there reported an error.
 
@@ -166,7 +183,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
               head_param: Optional[Union[torch.Tensor, Sequence[float]]] = None,
               sig_bias: float = 0.0, out_scale: float = 1.0,
               out: Optional[torch.Tensor] = None, schedule: str = "dynamic",
-              cu_seqlens=None, return_lse: bool = False, wait_limit_ns: int = 0):
+              cu_seqlens=None, return_lse: bool = False, wait_limit_ns: int = 0,
+              split_kv: Optional[bool] = None):
     """Generic forward attention: ``norm(mask(mod(q.k * scale))) @ v``.
 
     ``q, k, v``: CUDA tensors ``[B, H, S, D]`` (bf16 / fp16; fp32 computed as
@@ -188,6 +206,11 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     ``wait_limit_ns``: limit of each in-kernel wait (0 = 2 s). A wait that
     runs out is reported by ``check_device_status``; tests use tiny values to
     exercise that path.
+    ``split_kv``: decode-shaped calls -- at most 32 rows per K/V head
+    (``(H // H_kv) * S_q``) and ``S_q <= 64`` -- run on the split-KV decode
+    kernel, which spreads the keys of each K/V head over many SMs; ``None``
+    chooses it for those shapes, ``False`` forces the tiled kernel, ``True``
+    requires the decode kernel.
     """
     if schedule not in ("dynamic", "static"):
         raise ValueError(f"unknown schedule {schedule!r}")
@@ -283,9 +306,26 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
         p.lse = lse.data_ptr()
     p.wait_limit_ns = int(wait_limit_ns)
 
+    decode_shape = (cu_seqlens is None and (H // Hkv) * S <= DECODE_MAX_ROWS and S <= 64)
+    if split_kv and not decode_shape:
+        raise ValueError("split_kv=True needs (H // H_kv) * S_q <= 32, S_q <= 64 and no "
+                         "cu_seqlens")
+    use_decode = decode_shape if split_kv is None else bool(split_kv)
+
     lib = N.load()
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev).cuda_stream
+        if use_decode:
+            nbytes = lib.chia_attn_decode_workspace_bytes(ctypes.byref(p))
+            if nbytes < 0:
+                raise ValueError("not a decode-shaped call")
+            ws = _decode_workspace(dev, stream, nbytes)
+            N.check(lib.chia_attn_decode(ctypes.byref(p), ctypes.c_void_p(ws.data_ptr()),
+                                         ws.numel(), ctypes.c_void_p(stream)),
+                    f"chia_attn_decode(norm={norm}, mod={mod}, mask={mask}, "
+                    f"q={tuple(q.shape)}, k={tuple(k.shape)})")
+            o = o.float() if in_dtype == torch.float32 else o
+            return (o, lse) if return_lse else o
         # one workspace per (device, stream): see _workspace
         p.workspace = _workspace(dev, stream).data_ptr() if schedule == "dynamic" else None
         N.check(lib.chia_attn_fwd(ctypes.byref(p), ctypes.c_void_p(stream)),

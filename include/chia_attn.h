@@ -202,6 +202,31 @@ CHIA_API int chia_attn_fwd(const chia_attn_params_t *params, void *stream);
  * output, status and all other fields are as for chia_attn_fwd. */
 CHIA_API int chia_attn_fwd_noalloc(const chia_attn_params_t *params, void *stream);
 
+/* Split-KV forward for decode-shaped calls: few query rows per K/V head
+ * (heads / heads_kv * seqlen_q <= 32, e.g. one new token of a grouped-query
+ * model) over a long key sequence. Same fields, same visibility rule and
+ * score modifications as chia_attn_fwd, and the same output (plus lse when
+ * given); seq_offsets must be NULL and params->workspace is ignored. The key
+ * range is split over many CTAs, each reading its keys and values once; the
+ * last CTA of each K/V head merges the splits' partial results. The
+ * reference has no counterpart: its operators take S_q == S_kv; this is the
+ * decode step of the same operators (Gemma-2 style softcap + sliding window
+ * included).
+ *
+ * workspace: device memory of at least chia_attn_decode_workspace_bytes()
+ * bytes, 256-byte aligned, zero-filled before its first use. Its first
+ * 256 KiB hold the merge counters, which every call leaves zeroed again, so
+ * one workspace serves calls of any shape that fit in it. Calls that share a
+ * workspace must not overlap on the GPU. Returns CHIA_ERR_UNSUPPORTED for
+ * calls outside the decode shape (the caller then uses chia_attn_fwd) and
+ * for more than 65535 (batch, K/V head) pairs. */
+CHIA_API int chia_attn_decode(const chia_attn_params_t *params, void *workspace,
+                              int64_t workspace_bytes, void *stream);
+
+/* Workspace bytes chia_attn_decode needs for params on the current device
+ * (host-only arithmetic); -1 when params are invalid or not decode-shaped. */
+CHIA_API int64_t chia_attn_decode_workspace_bytes(const chia_attn_params_t *params);
+
 /* Number of visible (i, j) pairs of the mask described by params for one
  * (batch, head) pair -- the mask-aware FLOP count is 4 * D * pairs * B * H.
  * Host-only integer arithmetic; needs no GPU. Returns -1 on bad params and

@@ -546,3 +546,120 @@ def test_wait_that_runs_out_is_reported_and_the_device_recovers(cuda, D):
     assert int(ops._workspace(dev).abs().sum()) == 0
     check(cp.softcap_gemma2(qd, kd, vd), oracle.run_op("softcap_gemma2", q, k, v),
           "after a timeout")
+
+
+# ------------------------------------------------------ split-KV decode path
+def _decode_ref(op, q, k, v, okw, off):
+    """Oracle of a decode-shaped call: the reference operator's mask, mod and
+    normaliser with query row i at key position i + off (grouped K/V heads
+    repeated per query head)."""
+    from oracle import eager
+    H, Hkv = q.shape[1], k.shape[1]
+    kr, vr = (x.repeat_interleave(H // Hkv, dim=1) for x in (k, v))
+    spec = {
+        "softcap_gemma2": dict(norm="softmax", mod=lambda s, h, i, j: torch.tanh(s / 30.0) * 30.0),
+        "bias_alibi": dict(norm="softmax",
+                           mod=lambda s, h, i, j: s + okw["slopes"][h] * (j - (i + off)).float()),
+        "temp_perhead": dict(norm="softmax", mod=lambda s, h, i, j: s * okw["temps"][h]),
+        "sigmoid_attn": dict(norm="sigmoid", mod=lambda s, h, i, j: s + okw.get("bias", 0.0)),
+        "relu_attn": dict(norm="relu", mod=None),
+        "plain": dict(norm="softmax", mod=None),
+    }[op]
+    out = eager._eval(q, kr, vr, maskfn=lambda i, j: j <= i + off, **spec)
+    return out * okw.get("out_scale", 1.0) if op == "relu_attn" else out
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("Sq,H,Hkv,Skv", [(1, 8, 1, 3000), (1, 4, 4, 777), (4, 8, 2, 2049),
+                                          (2, 32, 2, 5000)])
+@pytest.mark.parametrize("op", ["plain", "softcap_gemma2", "bias_alibi", "temp_perhead",
+                                "sigmoid_attn", "relu_attn"])
+def test_split_kv_decode_matches_oracle(cuda, op, Sq, H, Hkv, Skv, D, dtype):
+    """Decode-shaped calls (rows per K/V head = H / H_kv * S_q <= 32) take the
+    split-KV kernel: query row i sits at key position Skv - Sq + i (causal,
+    bottom-right aligned), grouped K/V heads, every score modification."""
+    off = Skv - Sq
+    q, _, _ = gen(2, H, Sq, D, dtype, seed=Sq + H + D)
+    _, k, v = gen(2, Hkv, Skv, D, dtype, seed=Skv + D)
+    okw = {"bias_alibi": dict(slopes=cp.alibi_slopes_geometric(H)),
+           "temp_perhead": dict(temps=1.0 / _tau(H)),
+           "sigmoid_attn": dict(bias=-math.log(Skv)),
+           "relu_attn": dict(out_scale=1.0 / Skv)}.get(op, {})
+    kw = dict(norm={"sigmoid_attn": "sigmoid", "relu_attn": "relu"}.get(op, "softmax"),
+              mod={"softcap_gemma2": "softcap", "bias_alibi": "alibi",
+                   "temp_perhead": "temp"}.get(op, "none"),
+              mask=cp.Mask(left=-1, right=off))
+    if op == "bias_alibi":
+        kw["head_param"] = okw["slopes"]
+    if op == "temp_perhead":
+        kw["head_param"] = okw["temps"]
+    if op == "sigmoid_attn":
+        kw["sig_bias"] = okw["bias"]
+    if op == "relu_attn":
+        kw["out_scale"] = okw["out_scale"]
+    dev = torch.device("cuda", 0)
+    out = cp.attention(q.to(dev), k.to(dev), v.to(dev), split_kv=True, **kw)
+    torch.cuda.synchronize()
+    check(out, _decode_ref(op, q, k, v, okw, off), f"{op} Sq={Sq} H={H}/{Hkv} Skv={Skv}")
+
+
+@pytest.mark.parametrize("op,kw", [("bias_sliding_window", dict(window=100)),
+                                   ("bias_local", dict(window=64)),
+                                   ("bias_block_diagonal", dict(block=40)),
+                                   ("bias_dilated", dict(dilation=3)),
+                                   ("bias_prefix_lm", dict(prefix=20)),
+                                   ("softcap_gemma2", dict(cap=50.0, causal=False))])
+def test_split_kv_decode_masks(cuda, op, kw):
+    """Every mask shape through the decode kernel, on rows 0..S_q-1 of the
+    reference operators (top-left aligned, S_q < S_kv), against the oracle
+    and against the tiled kernel."""
+    H, Sq, Skv, D = 4, 30, 1500, 128   # 30 rows per K/V head: decode-shaped
+    q, _, _ = gen(1, H, Sq, D, torch.bfloat16, seed=101)
+    _, k, v = gen(1, H, Skv, D, torch.bfloat16, seed=102)
+    dev = torch.device("cuda", 0)
+    mask = cp.op_config(op, **kw)
+    mod = "softcap" if op == "softcap_gemma2" else "none"
+    extra = dict(softcap=kw["cap"]) if op == "softcap_gemma2" else {}
+    out = cp.attention(q.to(dev), k.to(dev), v.to(dev), mask=mask, mod=mod, split_kv=True,
+                       **extra)
+    tiled = cp.attention(q.to(dev), k.to(dev), v.to(dev), mask=mask, mod=mod, split_kv=False,
+                         **extra)
+    torch.cuda.synchronize()
+    from oracle import eager
+    i_ = torch.arange(Sq).view(-1, 1)
+    j_ = torch.arange(Skv).view(1, -1)
+    band = torch.ones(Sq, Skv, dtype=torch.bool)
+    if mask.left >= 0:
+        band &= (i_ - j_) <= mask.left
+    if mask.right >= 0:
+        band &= (j_ - i_) <= mask.right
+    if mask.block > 0:
+        band &= (i_ // mask.block) == (j_ // mask.block)
+    band &= ((i_ - j_) % mask.dilation) == 0
+    vis = band | (j_ < mask.prefix)
+    modf = (lambda s, h, i, j: torch.tanh(s / kw["cap"]) * kw["cap"]) if extra else None
+    ref = torch.nan_to_num(eager._eval(q, k, v, maskfn=lambda i, j: vis[i.flatten()][:, j.flatten()],
+                                       mod=modf), nan=0.0)
+    check(out, ref, f"{op} decode")
+    check(tiled, ref, f"{op} tiled")
+
+
+def test_split_kv_decode_long_gqa_and_lse(cuda):
+    """One new token per sequence over 8192 cached keys, 32 query heads on 4
+    K/V heads (GQA 8:1): sampled heads against the oracle, and the decode
+    kernel's log-sum-exp against the oracle's."""
+    B, H, Hkv, Skv, D = 4, 32, 4, 8192, 128
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(111)
+    q = torch.randn(B, H, 1, D, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, Skv, D, generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn(B, Hkv, Skv, D, generator=g, device=dev).to(torch.bfloat16)
+    out, lse = cp.attention(q, k, v, mask=cp.Mask(left=-1, right=Skv - 1), return_lse=True)
+    torch.cuda.synchronize()
+    for b, h in ((0, 0), (1, 9), (3, 31)):
+        hk = h // (H // Hkv)
+        qs, ks, vs = q[b:b + 1, h:h + 1].cpu(), k[b:b + 1, hk:hk + 1].cpu(), v[b:b + 1, hk:hk + 1].cpu()
+        ref, ref_lse = oracle.run_op_lse("softcap_gemma2", qs, ks, vs, cap=1e30, causal=False)
+        check(out[b:b + 1, h:h + 1], ref, f"head ({b},{h})")
+        assert abs(lse[b, h, 0].item() - ref_lse[0, 0, 0].item()) < 1e-3
