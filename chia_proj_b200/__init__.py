@@ -13,6 +13,7 @@ from .ops import (  # noqa: F401
     Mask,
     alibi_slopes_geometric,
     attention,
+    attention_backward,
     bias_alibi,
     bias_block_diagonal,
     bias_dilated,

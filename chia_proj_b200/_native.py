@@ -42,6 +42,8 @@ EXPORTED_SYMBOLS = (
     "chia_attn_abi_version",
     "chia_attn_decode",
     "chia_attn_decode_workspace_bytes",
+    "chia_attn_bwd",
+    "chia_attn_bwd_workspace_bytes",
 )
 
 
@@ -86,6 +88,21 @@ class AttnParams(ctypes.Structure):
     ]
 
 
+class AttnGrads(ctypes.Structure):
+    """Mirror of ``chia_attn_grads_t`` (include/chia_attn.h)."""
+
+    _fields_ = [
+        ("dout", ctypes.c_void_p),
+        ("dout_stride", ctypes.c_int64 * 3),
+        ("dq", ctypes.c_void_p),
+        ("dk", ctypes.c_void_p),
+        ("dv", ctypes.c_void_p),
+        ("dq_stride", ctypes.c_int64 * 3),
+        ("dk_stride", ctypes.c_int64 * 3),
+        ("dv_stride", ctypes.c_int64 * 3),
+    ]
+
+
 class ChiaError(RuntimeError):
     """A non-zero ``chia_status`` returned by the library."""
 
@@ -120,6 +137,11 @@ def load() -> ctypes.CDLL:
             lib.chia_attn_decode.restype = ctypes.c_int
             lib.chia_attn_decode_workspace_bytes.argtypes = [ctypes.POINTER(AttnParams)]
             lib.chia_attn_decode_workspace_bytes.restype = ctypes.c_int64
+            lib.chia_attn_bwd.argtypes = [ctypes.POINTER(AttnParams), ctypes.POINTER(AttnGrads),
+                                          ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
+            lib.chia_attn_bwd.restype = ctypes.c_int
+            lib.chia_attn_bwd_workspace_bytes.argtypes = [ctypes.POINTER(AttnParams)]
+            lib.chia_attn_bwd_workspace_bytes.restype = ctypes.c_int64
             lib.chia_attn_visible_pairs.argtypes = [ctypes.POINTER(AttnParams)]
             lib.chia_attn_visible_pairs.restype = ctypes.c_int64
             lib.chia_attn_tile_plan.argtypes = [

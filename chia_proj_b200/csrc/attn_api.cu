@@ -22,6 +22,7 @@
 #include <mutex>
 
 #include "../../include/chia_attn.h"
+#include "bwd_sm100.cuh"
 #include "decode_sm100.cuh"
 #include "fmha2_sm100.cuh"
 
@@ -387,9 +388,182 @@ int launch_decode_rp(int rp, const chia::DecodeArgs &a, dim3 grid, cudaStream_t 
   return rp == 16 ? launch_decode<D, 16, BF16>(a, grid, s) : launch_decode<D, 32, BF16>(a, grid, s);
 }
 
+// ------------------------------------------------------------- backward
+template <int D, bool BF16, int KIND>
+int launch_bwd(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
+               const CUtensorMap &mdo, const chia::BwdArgs &a, int grid, cudaStream_t s) {
+  using Cfg = chia::BwdConfig<D>;
+  auto kern = chia::fmha_bwd_kernel<D, BF16, KIND>;
+  static std::atomic<uint32_t> configured{0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHIA_ERR_NO_DEVICE;
+  const uint32_t bit = 1u << (dev & 31);
+  if (!(configured.load(std::memory_order_acquire) & bit)) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_ALLOC) !=
+        cudaSuccess)
+      return CHIA_ERR_LAUNCH;
+    configured.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_ALLOC, s>>>(mq, mk, mv, mdo, a);
+  return cudaGetLastError() == cudaSuccess ? CHIA_OK : CHIA_ERR_LAUNCH;
+}
+
+template <int D, bool BF16>
+int launch_bwd_kind(int kind, const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
+                    const CUtensorMap &mdo, const chia::BwdArgs &a, int grid, cudaStream_t s) {
+  switch (kind) {
+    case chia::KIND_SOFTMAX: return launch_bwd<D, BF16, chia::KIND_SOFTMAX>(mq, mk, mv, mdo, a, grid, s);
+    case chia::KIND_SOFTCAP: return launch_bwd<D, BF16, chia::KIND_SOFTCAP>(mq, mk, mv, mdo, a, grid, s);
+    case chia::KIND_ALIBI: return launch_bwd<D, BF16, chia::KIND_ALIBI>(mq, mk, mv, mdo, a, grid, s);
+    case chia::KIND_SIGMOID: return launch_bwd<D, BF16, chia::KIND_SIGMOID>(mq, mk, mv, mdo, a, grid, s);
+    case chia::KIND_RELU: return launch_bwd<D, BF16, chia::KIND_RELU>(mq, mk, mv, mdo, a, grid, s);
+  }
+  return CHIA_ERR_INVALID_ARGUMENT;
+}
+
+struct BwdLayout {
+  int64_t rows, off_dq, bytes;
+};
+
+BwdLayout bwd_layout(const chia_attn_params_t *p) {
+  BwdLayout l;
+  l.rows = p->batch * p->heads * p->seqlen_q;
+  auto up256 = [](int64_t x) { return (x + 255) / 256 * 256; };
+  l.off_dq = up256(l.rows * 4);                       // delta
+  l.bytes = l.off_dq + up256(l.rows * p->head_dim * 4);  // fp32 dq accumulator
+  return l;
+}
+
+bool strides_ok(const int64_t *st) {
+  for (int d = 0; d < 3; ++d)
+    if (st[d] < 0 || st[d] % 8 != 0) return false;
+  return true;
+}
+
 }  // namespace
 
 extern "C" {
+
+int64_t chia_attn_bwd_workspace_bytes(const chia_attn_params_t *p) {
+  if (validate(p) != CHIA_OK) return -1;
+  return bwd_layout(p).bytes;
+}
+
+int chia_attn_bwd(const chia_attn_params_t *p, const chia_attn_grads_t *gr, void *workspace,
+                  int64_t workspace_bytes, void *stream) {
+  const int v = validate(p);
+  if (v != CHIA_OK) return v;
+  if (gr == nullptr || !gr->dout || !gr->dq || !gr->dk || !gr->dv) return CHIA_ERR_INVALID_ARGUMENT;
+  if (p->seq_offsets != nullptr) return CHIA_ERR_UNSUPPORTED;
+  if (p->norm == CHIA_NORM_SOFTMAX && p->lse == nullptr) return CHIA_ERR_INVALID_ARGUMENT;
+  if (!aligned16(gr->dout) || !aligned16(gr->dq) || !aligned16(gr->dk) || !aligned16(gr->dv))
+    return CHIA_ERR_MISALIGNED;
+  if (!strides_ok(gr->dout_stride) || !strides_ok(gr->dq_stride) || !strides_ok(gr->dk_stride) ||
+      !strides_ok(gr->dv_stride))
+    return CHIA_ERR_MISALIGNED;
+  const BwdLayout lay = bwd_layout(p);
+  if (workspace == nullptr || workspace_bytes < lay.bytes) return CHIA_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return CHIA_ERR_MISALIGNED;
+  int dev = 0, major = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CHIA_ERR_NO_DEVICE;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      major != 10)
+    return CHIA_ERR_NO_DEVICE;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms < 1)
+    return CHIA_ERR_NO_DEVICE;
+
+  Derived dv;
+  derive(p, dv);
+  const MaskGeom &g = dv.geom;
+  const int D = p->head_dim;
+  const int64_t hkv = p->heads_kv > 0 ? p->heads_kv : p->heads;
+  const bool bf16 = p->dtype == CHIA_DTYPE_BF16;
+  const int kind = kind_of(p);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t *ws = static_cast<uint8_t *>(workspace);
+  float *delta = reinterpret_cast<float *>(ws);
+  float *dq_acc = reinterpret_cast<float *>(ws + lay.off_dq);
+
+  // 1. delta = rowsum(dout * o) (softmax kinds) and a zeroed dq accumulator
+  {
+    const int64_t blocks = (lay.rows * 32 + 255) / 256;
+    if (blocks > 0x7fffffffLL) return CHIA_ERR_UNSUPPORTED;
+    const bool want = p->norm == CHIA_NORM_SOFTMAX;
+#define CHIA_PREP(DD, BB)                                                                        \
+  chia::bwd_prep_kernel<DD, BB><<<static_cast<unsigned>(blocks), 256, 0, s>>>(                    \
+      p->o, gr->dout, p->o_stride[0], p->o_stride[1], p->o_stride[2], gr->dout_stride[0],        \
+      gr->dout_stride[1], gr->dout_stride[2], static_cast<int32_t>(p->heads), p->seqlen_q, delta, \
+      dq_acc, lay.rows, want)
+    if (D == 128) {
+      if (bf16) CHIA_PREP(128, true); else CHIA_PREP(128, false);
+    } else {
+      if (bf16) CHIA_PREP(64, true); else CHIA_PREP(64, false);
+    }
+#undef CHIA_PREP
+    if (cudaGetLastError() != cudaSuccess) return CHIA_ERR_LAUNCH;
+  }
+  // 2. the tensor-core kernel
+  CUtensorMap mq, mk, mv, mdo;
+  if (!encode_map(&mq, p->q, p->dtype, D, g.sq, dv.vdil, p->heads, p->batch, p->q_stride) ||
+      !encode_map(&mk, p->k, p->dtype, D, g.skv, dv.vdil, hkv, p->batch, p->k_stride) ||
+      !encode_map(&mv, p->v, p->dtype, D, g.skv, dv.vdil, hkv, p->batch, p->v_stride) ||
+      !encode_map(&mdo, gr->dout, p->dtype, D, g.sq, dv.vdil, p->heads, p->batch,
+                  gr->dout_stride))
+    return CHIA_ERR_LAUNCH;
+  chia::BwdArgs a{};
+  a.mask = g;
+  a.heads = static_cast<int32_t>(p->heads);
+  a.heads_kv = static_cast<int32_t>(hkv);
+  a.group = static_cast<int32_t>(p->heads / hkv);
+  a.vdil = dv.vdil;
+  const int64_t n_qt = (g.sq + 127) / 128, n_kt = (g.skv + 127) / 128;
+  const int64_t n_units = n_kt * p->batch * hkv * dv.vdil;
+  if (n_units > 0x7fffffffLL || n_qt > 0x7fffffffLL) return CHIA_ERR_UNSUPPORTED;
+  a.n_qt = static_cast<int32_t>(n_qt);
+  a.n_kt = static_cast<int32_t>(n_kt);
+  a.n_units = static_cast<int32_t>(n_units);
+  a.score_scale = p->scale;
+  a.softcap = p->softcap;
+  a.sig_bias = p->sig_bias;
+  a.out_scale = p->out_scale;
+  a.head_param = (p->mod == CHIA_MOD_ALIBI || p->mod == CHIA_MOD_TEMP) ? p->head_param : nullptr;
+  a.lse = p->lse;
+  a.delta = delta;
+  a.dq_acc = dq_acc;
+  a.dk = gr->dk;
+  a.dv = gr->dv;
+  a.dk_sb = gr->dk_stride[0]; a.dk_sh = gr->dk_stride[1]; a.dk_ss = gr->dk_stride[2];
+  a.dv_sb = gr->dv_stride[0]; a.dv_sh = gr->dv_stride[1]; a.dv_ss = gr->dv_stride[2];
+  a.sq_real = p->seqlen_q;
+  a.status = p->status;
+  a.timeout_ns = p->wait_limit_ns > 0 ? p->wait_limit_ns : kDefaultTimeoutNs;
+  a.drain_ns = kDrainNs;
+  const int grid = static_cast<int>(n_units < sms ? n_units : sms);
+  int r;
+  if (D == 128)
+    r = bf16 ? launch_bwd_kind<128, true>(kind, mq, mk, mv, mdo, a, grid, s)
+             : launch_bwd_kind<128, false>(kind, mq, mk, mv, mdo, a, grid, s);
+  else
+    r = bf16 ? launch_bwd_kind<64, true>(kind, mq, mk, mv, mdo, a, grid, s)
+             : launch_bwd_kind<64, false>(kind, mq, mk, mv, mdo, a, grid, s);
+  if (r != CHIA_OK) return r;
+  // 3. dq = the fp32 accumulator rounded to the input type
+  {
+    const int64_t blocks = (lay.rows * 32 + 255) / 256;
+#define CHIA_DQ(DD, BB)                                                                   \
+  chia::bwd_dq_kernel<DD, BB><<<static_cast<unsigned>(blocks), 256, 0, s>>>(               \
+      dq_acc, gr->dq, gr->dq_stride[0], gr->dq_stride[1], gr->dq_stride[2],                \
+      static_cast<int32_t>(p->heads), p->seqlen_q, lay.rows)
+    if (D == 128) {
+      if (bf16) CHIA_DQ(128, true); else CHIA_DQ(128, false);
+    } else {
+      if (bf16) CHIA_DQ(64, true); else CHIA_DQ(64, false);
+    }
+#undef CHIA_DQ
+    if (cudaGetLastError() != cudaSuccess) return CHIA_ERR_LAUNCH;
+  }
+  return CHIA_OK;
+}
 
 int64_t chia_attn_decode_workspace_bytes(const chia_attn_params_t *p) {
   if (validate(p) != CHIA_OK) return -1;

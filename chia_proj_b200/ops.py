@@ -37,7 +37,7 @@ __all__ = [
     "softcap_gemma2", "bias_sliding_window", "bias_local", "bias_alibi",
     "bias_block_diagonal", "bias_dilated", "bias_prefix_lm", "temp_perhead",
     "sigmoid_attn", "relu_attn", "alibi_slopes_geometric", "reference_alibi_slopes",
-    "reference_temps", "check_device_status",
+    "reference_temps", "check_device_status", "attention_backward",
 ]
 
 
@@ -212,6 +212,13 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
     chooses it for those shapes, ``False`` forces the tiled kernel, ``True``
     requires the decode kernel.
     """
+    if (torch.is_grad_enabled() and any(isinstance(t, torch.Tensor) and t.requires_grad
+                                        for t in (q, k, v))):
+        if out is not None or cu_seqlens is not None:
+            raise ValueError("out= and cu_seqlens= do not support gradients")
+        o, lse = _AttentionFn.apply(q, k, v, norm, mod, mask, scale, softcap, head_param,
+                                    sig_bias, out_scale)
+        return (o, lse) if return_lse else o
     if schedule not in ("dynamic", "static"):
         raise ValueError(f"unknown schedule {schedule!r}")
     if norm not in _NORMS or mod not in _MODS:
@@ -332,6 +339,105 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
                 f"chia_attn_fwd(norm={norm}, mod={mod}, mask={mask}, shape={tuple(q.shape)})")
     o = o.float() if in_dtype == torch.float32 else o
     return (o, lse) if return_lse else o
+
+
+# ---------------------------------------------------------------------------
+# backward pass
+# ---------------------------------------------------------------------------
+_bwd_workspaces: Dict[tuple, torch.Tensor] = {}
+
+
+def _params_for(q, k, v, o, *, norm, mod, mask, scale, softcap, hp, sig_bias, out_scale,
+                lse=None) -> "N.AttnParams":
+    B, H, S, D = q.shape
+    p = N.AttnParams()
+    p.abi_version = N.ABI_VERSION
+    p.dtype = N.DTYPE_BF16 if q.dtype == torch.bfloat16 else N.DTYPE_F16
+    p.head_dim = D
+    p.norm, p.mod = _NORMS[norm], _MODS[mod]
+    p.batch, p.heads, p.seqlen_q, p.seqlen_kv = B, H, S, k.shape[2]
+    p.heads_kv = k.shape[1]
+    p.q, p.k, p.v, p.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr()
+    for field, t in (("q_stride", q), ("k_stride", k), ("v_stride", v), ("o_stride", o)):
+        getattr(p, field)[:] = t.stride()[:3]
+    p.scale = (1.0 / math.sqrt(D)) if scale is None else float(scale)
+    p.softcap, p.sig_bias, p.out_scale = float(softcap), float(sig_bias), float(out_scale)
+    p.head_param = hp.data_ptr() if hp is not None else None
+    p.win_left, p.win_right = mask.left, mask.right
+    p.block, p.prefix, p.dilation = mask.block, mask.prefix, mask.dilation
+    p.status = _status_word(q.device).data_ptr()
+    p.lse = lse.data_ptr() if lse is not None else None
+    return p
+
+
+def attention_backward(dout, q, k, v, out, lse, *, norm="softmax", mod="none", mask=CAUSAL,
+                       scale=None, softcap=30.0, head_param=None, sig_bias=0.0, out_scale=1.0):
+    """Gradients ``(dq, dk, dv)`` of ``attention(q, k, v, ...)`` given the
+    upstream gradient ``dout``, the forward's output ``out`` and (softmax)
+    its log-sum-exp ``lse`` (``attention(..., return_lse=True)``). One call
+    of ``chia_attn_bwd``; ``dk``, ``dv`` have the K/V heads of ``k``, ``v``."""
+    q, k, v, out, dout = (_prep(t) for t in (q, k, v, out, dout))
+    dev = q.device
+    if not (q.dtype == k.dtype == v.dtype == out.dtype == dout.dtype):
+        raise ValueError("q, k, v, out, dout must share a dtype")
+    if norm == "softmax" and lse is None:
+        raise ValueError("the softmax backward needs the forward's lse")
+    hp = None
+    if mod in ("alibi", "temp"):
+        hp = (_cached_default(mod, q.shape[1], dev) if head_param is None
+              else _param_tensor(head_param, q.shape[1], dev))
+    p = _params_for(q, k, v, out, norm=norm, mod=mod, mask=mask.validate(), scale=scale,
+                    softcap=softcap, hp=hp, sig_bias=sig_bias, out_scale=out_scale,
+                    lse=lse.contiguous() if lse is not None else None)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    g = N.AttnGrads()
+    g.dout = dout.data_ptr()
+    g.dout_stride[:] = dout.stride()[:3]
+    g.dq, g.dk, g.dv = dq.data_ptr(), dk.data_ptr(), dv.data_ptr()
+    g.dq_stride[:] = dq.stride()[:3]
+    g.dk_stride[:] = dk.stride()[:3]
+    g.dv_stride[:] = dv.stride()[:3]
+    lib = N.load()
+    nbytes = lib.chia_attn_bwd_workspace_bytes(ctypes.byref(p))
+    if nbytes < 0:
+        raise ValueError("invalid backward parameters")
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        key = (dev.index, int(stream))
+        ws = _bwd_workspaces.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+            _bwd_workspaces[key] = ws
+        N.check(lib.chia_attn_bwd(ctypes.byref(p), ctypes.byref(g), ctypes.c_void_p(ws.data_ptr()),
+                                  ws.numel(), ctypes.c_void_p(stream)),
+                f"chia_attn_bwd(norm={norm}, mod={mod}, mask={mask}, shape={tuple(q.shape)})")
+    return dq, dk, dv
+
+
+class _AttentionFn(torch.autograd.Function):
+    """Autograd for ``attention``: the forward kernel (with the log-sum-exp
+    for softmax), the backward kernel for the gradients of q, k and v.
+    Per-head parameters and scalars are not differentiated."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, norm, mod, mask, scale, softcap, head_param, sig_bias, out_scale):
+        kw = dict(norm=norm, mod=mod, mask=mask, scale=scale, softcap=softcap,
+                  head_param=head_param, sig_bias=sig_bias, out_scale=out_scale)
+        with torch.no_grad():
+            if norm == "softmax":
+                o, lse = attention(q, k, v, return_lse=True, split_kv=False, **kw)
+            else:
+                o, lse = attention(q, k, v, split_kv=False, **kw), None
+        ctx.save_for_backward(q, k, v, o, lse)
+        ctx.kw = kw
+        ctx.mark_non_differentiable(*(x for x in (lse,) if x is not None))
+        return o, lse
+
+    @staticmethod
+    def backward(ctx, dout, dlse):
+        q, k, v, o, lse = ctx.saved_tensors
+        dq, dk, dv = attention_backward(dout.to(o.dtype), q, k, v, o, lse, **ctx.kw)
+        return dq, dk, dv, None, None, None, None, None, None, None, None
 
 
 # ---------------------------------------------------------------------------

@@ -227,6 +227,40 @@ CHIA_API int chia_attn_decode(const chia_attn_params_t *params, void *workspace,
  * (host-only arithmetic); -1 when params are invalid or not decode-shaped. */
 CHIA_API int64_t chia_attn_decode_workspace_bytes(const chia_attn_params_t *params);
 
+/* Gradient tensors of chia_attn_bwd: [B, H, S, D] like q, k, v, o (K/V
+ * gradients with heads_kv heads), 16-bit of params->dtype, unit stride on D,
+ * strides in elements, multiples of 8; pointers 16-byte aligned. */
+typedef struct chia_attn_grads {
+  const void *dout;     /* upstream gradient of the output o           */
+  int64_t dout_stride[3];
+  void *dq;             /* written: gradient of q                      */
+  void *dk;             /* written: gradient of k                      */
+  void *dv;             /* written: gradient of v                      */
+  int64_t dq_stride[3];
+  int64_t dk_stride[3];
+  int64_t dv_stride[3];
+} chia_attn_grads_t;
+
+/* Backward pass of chia_attn_fwd: dq, dk, dv for the same params (q, k, v,
+ * the forward's output in params->o and, for CHIA_NORM_SOFTMAX, the
+ * forward's log-sum-exp in params->lse). Every score modification, mask and
+ * normaliser of chia_attn_fwd, grouped K/V heads (dk, dv summed over the
+ * query heads of a group) and the dilated residue-class path; packed
+ * sequences (seq_offsets) return CHIA_ERR_UNSUPPORTED. The reference is
+ * forward only (README.md); the gradients are those of its eager functions
+ * (extra_bench.py:32-62, sigmoid_fix.py:34-40) differentiated exactly, with
+ * P and dS rounded to the input type for the tensor cores.
+ *
+ * workspace: device memory of chia_attn_bwd_workspace_bytes() bytes,
+ * 256-byte aligned, no initial contents needed (fp32 dq accumulator and
+ * the row sums of dout * o). Calls that share a workspace must not overlap
+ * on the GPU. */
+CHIA_API int chia_attn_bwd(const chia_attn_params_t *params, const chia_attn_grads_t *grads,
+                           void *workspace, int64_t workspace_bytes, void *stream);
+
+/* Workspace bytes of chia_attn_bwd (host-only); -1 for invalid params. */
+CHIA_API int64_t chia_attn_bwd_workspace_bytes(const chia_attn_params_t *params);
+
 /* Number of visible (i, j) pairs of the mask described by params for one
  * (batch, head) pair -- the mask-aware FLOP count is 4 * D * pairs * B * H.
  * Host-only integer arithmetic; needs no GPU. Returns -1 on bad params and
