@@ -378,6 +378,7 @@ def headline_suite(device, rank: int = 0, ws: int = 1, profile_launches: bool = 
                           "softcap_gemma2": c1}
         del sets
         out["decode"] = decode_bench(device)
+        out["backward"] = backward_bench(device)
     out["configs_clocks"] = clk.summary()
     torch.cuda.empty_cache()
     return out
@@ -419,6 +420,48 @@ def decode_bench(device, iters: int = 20):
                      "frac_hbm": round(by / ms / 1e6 / hbm, 3),
                      "tflops": round(fl / ms / 1e9, 2)}
     del sets
+    return res
+
+
+def backward_bench(device, iters: int = 10):
+    """Backward pass (dQ, dK, dV) at the headline shape B4 H16 S4096 D128
+    bf16: the kernel call chia_attn_bwd given the forward's output and
+    log-sum-exp. Mask-aware FLOPs of the backward: five products (S, dP, dV,
+    dK, dQ) of 2 * D per visible pair, 10 * D * pairs * B * H."""
+    import chia_proj_b200 as cp
+    B, H, Sx, Dx = 4, 16, 4096, 128
+    g = torch.Generator(device=device).manual_seed(17)
+    q, k, v, do = (torch.randn(B, H, Sx, Dx, generator=g, device=device).to(torch.bfloat16)
+                   for _ in range(4))
+    pk, _ = peaks()
+    p_tensor = pk.get("bf16_tflops", FALLBACK["bf16_tflops"])
+    res = {"shape": {"B": B, "H": H, "S": Sx, "D": Dx, "dtype": "bf16"}}
+    cases = {
+        "softcap_gemma2": (dict(mod="softcap", softcap=50.0, mask=cp.CAUSAL), cp.CAUSAL),
+        "bias_prefix_lm": (dict(mask=cp.op_config("bias_prefix_lm", prefix=1024)),
+                           cp.op_config("bias_prefix_lm", prefix=1024)),
+        "sigmoid_attn": (dict(norm="sigmoid", sig_bias=-math.log(Sx), mask=cp.FULL), cp.FULL),
+    }
+    for name, (kw, mask) in cases.items():
+        if kw.get("norm", "softmax") == "softmax":
+            o, lse = cp.attention(q, k, v, return_lse=True, **kw)
+        else:
+            o, lse = cp.attention(q, k, v, **kw), None
+        fn = lambda: cp.attention_backward(do, q, k, v, o, lse, **kw)
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        for _ in range(iters):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / iters
+        fl = 10 * Dx * cp.visible_pairs(mask, Sx) * B * H
+        res[name] = {"us": round(ms * 1e3, 1), "tflops": round(fl / ms / 1e9, 1),
+                     "frac": round(fl / ms / 1e9 / p_tensor, 3)}
+    del q, k, v, do
     return res
 
 

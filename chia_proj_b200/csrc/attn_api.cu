@@ -315,6 +315,7 @@ struct DecodePlan {
 
 constexpr int kDecodeMaxRows = 32;
 constexpr int64_t kDecodeMaxHeads = 65535;  // batch * K/V heads (grid y)
+constexpr int64_t kDecodeMaxSplits = 256;
 
 int decode_plan(const chia_attn_params_t *p, int sms, DecodePlan &pl) {
   if (p->seq_offsets != nullptr) return CHIA_ERR_UNSUPPORTED;
@@ -338,15 +339,18 @@ int decode_plan(const chia_attn_params_t *p, int sms, DecodePlan &pl) {
   pl.nkeys = khi >= klo ? khi - klo + 1 : 0;
   constexpr int TK = 64;
   const int64_t min_keys = 4 * TK;  // per split: amortises the Q load and the merge
-  int64_t splits = (4 * static_cast<int64_t>(sms) + pl.nkvh - 1) / pl.nkvh;
+  // about one wave of CTAs (two per SM fit): enough keys in flight per SM,
+  // and few partial results for the merge
+  int64_t splits = (2 * static_cast<int64_t>(sms) + pl.nkvh - 1) / pl.nkvh;
   const int64_t by_keys = (pl.nkeys + min_keys - 1) / min_keys;
   if (splits > by_keys) splits = by_keys;
+  if (splits > kDecodeMaxSplits) splits = kDecodeMaxSplits;  // the merge's weights fit in smem
   if (splits < 1) splits = 1;
   int64_t kps = (pl.nkeys + splits - 1) / splits;
   kps = (kps + TK - 1) / TK * TK;
   if (kps < TK) kps = TK;
   splits = pl.nkeys > 0 ? (pl.nkeys + kps - 1) / kps : 1;
-  if (kps > 0x7fffffff || splits > 0xffff) return CHIA_ERR_UNSUPPORTED;
+  if (kps > 0x7fffffff || splits > kDecodeMaxSplits) return CHIA_ERR_UNSUPPORTED;
   pl.kps = static_cast<int32_t>(kps);
   pl.splits = static_cast<int32_t>(splits);
   // Workspace: the tickets first, at a fixed place and size (one per possible

@@ -389,35 +389,75 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeArgs a) {
   __threadfence();
 
   // ---------------- the last split of the head merges all of them ----------------
+  // Every split's row maxima and sums go to shared memory in one round of
+  // loads; the weights 2^(m_s - M) follow per row; then each thread sums the
+  // splits' partial outputs for four columns of a row, loads issued together.
   const float *pml = a.part_ml + static_cast<int64_t>(kvh) * a.splits * RP * 2;
   const float *pob = a.part_o + static_cast<int64_t>(kvh) * a.splits * RP * D;
-  for (int e = t; e < a.rows * (D / 2); e += C::THREADS) {  // two columns per step
-    const int r = e / (D / 2), c2 = e % (D / 2);
+  float *wsm = reinterpret_cast<float *>(sm);  // [splits][RP] weights, then [RP] 1/L, [RP] M, [RP] L
+  const int nsw = a.splits * RP;
+  for (int e = t; e < nsw; e += C::THREADS) wsm[e] = __ldcg(pml + 2 * e);  // maxima
+  __syncthreads();
+  float *inv_s = wsm + nsw, *m_sm = inv_s + RP, *l_sm = m_sm + RP;
+  if (t < RP) {
     float M = -INFINITY;
     if (softmax)
-      for (int s2 = 0; s2 < a.splits; ++s2) M = fmaxf(M, __ldcg(pml + (s2 * RP + r) * 2));
-    float L = 0.f, o0 = 0.f, o1 = 0.f;
+      for (int s2 = 0; s2 < a.splits; ++s2) M = fmaxf(M, wsm[s2 * RP + t]);
+    float L = 0.f;
     for (int s2 = 0; s2 < a.splits; ++s2) {
       float wt = 1.f;
       if (softmax) {
-        const float ms = __ldcg(pml + (s2 * RP + r) * 2);
+        const float ms = wsm[s2 * RP + t];
         wt = ms == -INFINITY ? 0.f : ptx::ex2(ms - M);
-        L += wt * __ldcg(pml + (s2 * RP + r) * 2 + 1);
+        L += wt * __ldcg(pml + (s2 * RP + t) * 2 + 1);
       }
-      const float2 ov = __ldcg(reinterpret_cast<const float2 *>(pob + (s2 * RP + r) * D) + c2);
-      o0 = fmaf(wt, ov.x, o0);
-      o1 = fmaf(wt, ov.y, o1);
+      wsm[s2 * RP + t] = wt;
     }
     float inv = 1.f;
     if (softmax) inv = L > 0.f ? 1.f / L : 0.f;
     if (kind == 4) inv = a.out_scale;
+    inv_s[t] = inv;
+    m_sm[t] = M;
+    l_sm[t] = L;
+  }
+  __syncthreads();
+  for (int e = t; e < a.rows * (D / 4); e += C::THREADS) {  // four columns per step
+    const int r = e / (D / 4), c4 = e % (D / 4);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4 *src = reinterpret_cast<const float4 *>(pob + r * D) + c4;
+    constexpr int U4 = 4;
+    int s2 = 0;
+    for (; s2 + U4 <= a.splits; s2 += U4) {
+      float4 ov[U4];
+#pragma unroll
+      for (int uu = 0; uu < U4; ++uu) ov[uu] = __ldcg(src + (s2 + uu) * (RP * D / 4));
+#pragma unroll
+      for (int uu = 0; uu < U4; ++uu) {
+        const float wt = wsm[(s2 + uu) * RP + r];
+        acc.x = fmaf(wt, ov[uu].x, acc.x);
+        acc.y = fmaf(wt, ov[uu].y, acc.y);
+        acc.z = fmaf(wt, ov[uu].z, acc.z);
+        acc.w = fmaf(wt, ov[uu].w, acc.w);
+      }
+    }
+    for (; s2 < a.splits; ++s2) {
+      const float4 ov = __ldcg(src + s2 * (RP * D / 4));
+      const float wt = wsm[s2 * RP + r];
+      acc.x = fmaf(wt, ov.x, acc.x);
+      acc.y = fmaf(wt, ov.y, acc.y);
+      acc.z = fmaf(wt, ov.z, acc.z);
+      acc.w = fmaf(wt, ov.w, acc.w);
+    }
+    const float inv = inv_s[r];
     const int h = hk * a.group + r / a.sq, qi = r % a.sq;
     uint8_t *orow = reinterpret_cast<uint8_t *>(a.o) + 2 * (b * a.o_sb + h * a.o_sh + qi * a.o_ss);
-    *reinterpret_cast<uint32_t *>(orow + 4 * c2) = pack16<BF16>(o0 * inv, o1 * inv);
-    if (softmax && a.lse != nullptr && c2 == 0) {
+    *reinterpret_cast<uint2 *>(orow + 8 * c4) =
+        make_uint2(pack16<BF16>(acc.x * inv, acc.y * inv), pack16<BF16>(acc.z * inv, acc.w * inv));
+    if (softmax && a.lse != nullptr && c4 == 0) {
       constexpr float LN2 = 0.6931471805599453f;
+      const float L = l_sm[r];
       a.lse[(static_cast<int64_t>(b) * a.heads + h) * a.sq + qi] =
-          L > 0.f ? (M + __log2f(L)) * LN2 : -INFINITY;
+          L > 0.f ? (m_sm[r] + __log2f(L)) * LN2 : -INFINITY;
     }
   }
   if (t == 0) a.tickets[kvh] = 0;  // ready for the next launch

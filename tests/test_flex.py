@@ -112,6 +112,11 @@ def test_flex_attention_matches_the_oracle(cuda, op):
     g = torch.Generator().manual_seed(13)
     q, k, v = (torch.randn(1, H, S, D, generator=g).to(torch.bfloat16) for _ in range(3))
     score_mod, mask_mod = REF_FLEX[op]
+    # as in the reference, the per-head parameters the callables capture live
+    # on the device the call runs on
+    sl, te = SLOPES.to(cuda), TEMPS.to(cuda)
+    score_mod = {"temp_perhead": lambda sc, b, h, qi, kj: sc * te[h],
+                 "bias_alibi": lambda sc, b, h, qi, kj: sc + sl[h] * (kj - qi)}.get(op, score_mod)
     bm = flex.create_block_mask(mask_mod, None, None, S, S, device=cuda)
     out = flex.flex_attention(q.to(cuda), k.to(cuda), v.to(cuda), score_mod=score_mod,
                               block_mask=bm)
