@@ -465,6 +465,28 @@ def backward_bench(device, iters: int = 10):
     return res
 
 
+def profile_bwd_decode(device):
+    """One backward call (B4 H16 S4096 D128 bf16, softcap 50, causal) and one
+    decode call (the decode benchmark's shape), each after one untimed call."""
+    import chia_proj_b200 as cp
+    torch.cuda.set_device(device)
+    g = torch.Generator(device=device).manual_seed(17)
+    q, k, v, do = (torch.randn(4, 16, 4096, 128, generator=g, device=device).to(torch.bfloat16)
+                   for _ in range(4))
+    kw = dict(mod="softcap", softcap=50.0, mask=cp.CAUSAL)
+    o, lse = cp.attention(q, k, v, return_lse=True, **kw)
+    for _ in range(2):
+        cp.attention_backward(do, q, k, v, o, lse, **kw)
+    del q, k, v, do, o, lse
+    qd = torch.randn(8, 32, 1, 128, generator=g, device=device).to(torch.bfloat16)
+    kd, vd = (torch.randn(8, 4, 8192, 128, generator=g, device=device).to(torch.bfloat16)
+              for _ in range(2))
+    for _ in range(2):
+        cp.attention(qd, kd, vd, mask=cp.Mask(left=-1, right=8191))
+    torch.cuda.synchronize()
+    print(json.dumps({"profiled": ["fmha_bwd_kernel", "decode_kernel"]}))
+
+
 def preheat(step, seconds: float):
     """Untimed load before the warm-up steps, so that every N reaches the
     power state of a long run (at the 1 kW cap the SM clock settles lower
@@ -763,6 +785,9 @@ def main(argv=None):
                     help="run only the per-variant suite at the north-star shape (1 GPU)")
     ap.add_argument("--profile-launches", action="store_true",
                     help="launch each headline variant and config 2 once, untimed (ncu)")
+    ap.add_argument("--profile-bwd-decode", action="store_true",
+                    help="one backward call at the headline shape (softcap, causal) and one "
+                         "decode call of the decode benchmark, untimed (ncu)")
     ap.add_argument("--units", type=int, default=B_TOTAL * H_TOTAL,
                     help="(batch, head) units in the job; smaller values are for ncu captures")
     a = ap.parse_args(argv)
@@ -770,6 +795,8 @@ def main(argv=None):
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
     if a.impl == "reference":
         run_reference(a)
+    elif a.profile_bwd_decode:
+        profile_bwd_decode(torch.device("cuda", 0))
     elif a.suite_only or a.profile_launches:
         torch.cuda.set_device(0)
         print(json.dumps({"suite": headline_suite(torch.device("cuda", 0),

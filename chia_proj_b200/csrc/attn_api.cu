@@ -172,6 +172,25 @@ bool encode_map(CUtensorMap *map, const void *base, int dtype, int64_t D, int64_
   return r == CUDA_SUCCESS;
 }
 
+// fp32 [B, H, S, D] buffer (contiguous, real rows) viewed like encode_map
+// (D, S', vdil, H, B), box (32, 128, 1, 1, 1): 128 bytes per box row, 128-byte
+// swizzle. The backward pass adds its dQ tiles into it with TMA reductions.
+bool encode_map_f32(CUtensorMap *map, float *base, int64_t D, int64_t s_real, int64_t s_virtual,
+                    int vdil, int64_t H, int64_t B) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[5] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(s_virtual),
+                              static_cast<cuuint64_t>(vdil), static_cast<cuuint64_t>(H),
+                              static_cast<cuuint64_t>(B)};
+  const cuuint64_t row = static_cast<cuuint64_t>(D) * 4;
+  const cuuint64_t st[4] = {row * vdil, row, row * s_real, row * s_real * H};
+  const cuuint32_t box[5] = {32, 128, 1, 1, 1};
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, base, dims, st, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // ----------------------------------------------------------------- dispatch
 template <int D, bool BF16, int KIND, bool SEG>
 int launch_one(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
@@ -339,9 +358,9 @@ int decode_plan(const chia_attn_params_t *p, int sms, DecodePlan &pl) {
   pl.nkeys = khi >= klo ? khi - klo + 1 : 0;
   constexpr int TK = 64;
   const int64_t min_keys = 4 * TK;  // per split: amortises the Q load and the merge
-  // about one wave of CTAs (two per SM fit): enough keys in flight per SM,
-  // and few partial results for the merge
-  int64_t splits = (2 * static_cast<int64_t>(sms) + pl.nkvh - 1) / pl.nkvh;
+  // at most one wave of CTAs (two per SM fit): a second, partial wave would
+  // double the time; few partial results for the merge
+  int64_t splits = 2 * static_cast<int64_t>(sms) / pl.nkvh;
   const int64_t by_keys = (pl.nkeys + min_keys - 1) / min_keys;
   if (splits > by_keys) splits = by_keys;
   if (splits > kDecodeMaxSplits) splits = kDecodeMaxSplits;  // the merge's weights fit in smem
@@ -395,7 +414,8 @@ int launch_decode_rp(int rp, const chia::DecodeArgs &a, dim3 grid, cudaStream_t 
 // ------------------------------------------------------------- backward
 template <int D, bool BF16, int KIND>
 int launch_bwd(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
-               const CUtensorMap &mdo, const chia::BwdArgs &a, int grid, cudaStream_t s) {
+               const CUtensorMap &mdo, const CUtensorMap &mdq, const chia::BwdArgs &a, int grid,
+               cudaStream_t s) {
   using Cfg = chia::BwdConfig<D>;
   auto kern = chia::fmha_bwd_kernel<D, BF16, KIND>;
   static std::atomic<uint32_t> configured{0};
@@ -408,19 +428,25 @@ int launch_bwd(const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &
       return CHIA_ERR_LAUNCH;
     configured.fetch_or(bit, std::memory_order_acq_rel);
   }
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_ALLOC, s>>>(mq, mk, mv, mdo, a);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_ALLOC, s>>>(mq, mk, mv, mdo, mdq, a);
   return cudaGetLastError() == cudaSuccess ? CHIA_OK : CHIA_ERR_LAUNCH;
 }
 
 template <int D, bool BF16>
 int launch_bwd_kind(int kind, const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
-                    const CUtensorMap &mdo, const chia::BwdArgs &a, int grid, cudaStream_t s) {
+                    const CUtensorMap &mdo, const CUtensorMap &mdq, const chia::BwdArgs &a,
+                    int grid, cudaStream_t s) {
   switch (kind) {
-    case chia::KIND_SOFTMAX: return launch_bwd<D, BF16, chia::KIND_SOFTMAX>(mq, mk, mv, mdo, a, grid, s);
-    case chia::KIND_SOFTCAP: return launch_bwd<D, BF16, chia::KIND_SOFTCAP>(mq, mk, mv, mdo, a, grid, s);
-    case chia::KIND_ALIBI: return launch_bwd<D, BF16, chia::KIND_ALIBI>(mq, mk, mv, mdo, a, grid, s);
-    case chia::KIND_SIGMOID: return launch_bwd<D, BF16, chia::KIND_SIGMOID>(mq, mk, mv, mdo, a, grid, s);
-    case chia::KIND_RELU: return launch_bwd<D, BF16, chia::KIND_RELU>(mq, mk, mv, mdo, a, grid, s);
+    case chia::KIND_SOFTMAX:
+      return launch_bwd<D, BF16, chia::KIND_SOFTMAX>(mq, mk, mv, mdo, mdq, a, grid, s);
+    case chia::KIND_SOFTCAP:
+      return launch_bwd<D, BF16, chia::KIND_SOFTCAP>(mq, mk, mv, mdo, mdq, a, grid, s);
+    case chia::KIND_ALIBI:
+      return launch_bwd<D, BF16, chia::KIND_ALIBI>(mq, mk, mv, mdo, mdq, a, grid, s);
+    case chia::KIND_SIGMOID:
+      return launch_bwd<D, BF16, chia::KIND_SIGMOID>(mq, mk, mv, mdo, mdq, a, grid, s);
+    case chia::KIND_RELU:
+      return launch_bwd<D, BF16, chia::KIND_RELU>(mq, mk, mv, mdo, mdq, a, grid, s);
   }
   return CHIA_ERR_INVALID_ARGUMENT;
 }
@@ -507,12 +533,13 @@ int chia_attn_bwd(const chia_attn_params_t *p, const chia_attn_grads_t *gr, void
     if (cudaGetLastError() != cudaSuccess) return CHIA_ERR_LAUNCH;
   }
   // 2. the tensor-core kernel
-  CUtensorMap mq, mk, mv, mdo;
+  CUtensorMap mq, mk, mv, mdo, mdq;
   if (!encode_map(&mq, p->q, p->dtype, D, g.sq, dv.vdil, p->heads, p->batch, p->q_stride) ||
       !encode_map(&mk, p->k, p->dtype, D, g.skv, dv.vdil, hkv, p->batch, p->k_stride) ||
       !encode_map(&mv, p->v, p->dtype, D, g.skv, dv.vdil, hkv, p->batch, p->v_stride) ||
       !encode_map(&mdo, gr->dout, p->dtype, D, g.sq, dv.vdil, p->heads, p->batch,
-                  gr->dout_stride))
+                  gr->dout_stride) ||
+      !encode_map_f32(&mdq, dq_acc, D, p->seqlen_q, g.sq, dv.vdil, p->heads, p->batch))
     return CHIA_ERR_LAUNCH;
   chia::BwdArgs a{};
   a.mask = g;
@@ -545,11 +572,11 @@ int chia_attn_bwd(const chia_attn_params_t *p, const chia_attn_grads_t *gr, void
   const int grid = static_cast<int>(n_units < sms ? n_units : sms);
   int r;
   if (D == 128)
-    r = bf16 ? launch_bwd_kind<128, true>(kind, mq, mk, mv, mdo, a, grid, s)
-             : launch_bwd_kind<128, false>(kind, mq, mk, mv, mdo, a, grid, s);
+    r = bf16 ? launch_bwd_kind<128, true>(kind, mq, mk, mv, mdo, mdq, a, grid, s)
+             : launch_bwd_kind<128, false>(kind, mq, mk, mv, mdo, mdq, a, grid, s);
   else
-    r = bf16 ? launch_bwd_kind<64, true>(kind, mq, mk, mv, mdo, a, grid, s)
-             : launch_bwd_kind<64, false>(kind, mq, mk, mv, mdo, a, grid, s);
+    r = bf16 ? launch_bwd_kind<64, true>(kind, mq, mk, mv, mdo, mdq, a, grid, s)
+             : launch_bwd_kind<64, false>(kind, mq, mk, mv, mdo, mdq, a, grid, s);
   if (r != CHIA_OK) return r;
   // 3. dq = the fp32 accumulator rounded to the input type
   {

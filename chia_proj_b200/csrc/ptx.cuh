@@ -99,6 +99,17 @@ __device__ __forceinline__ void tma_store_5d(const CUtensorMap *map, uint32_t sr
       "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
       : "memory");
 }
+// TMA tensor reduce-add (fp32) of a box from this CTA's shared memory into
+// global memory (bulk async-group of the issuing thread); out-of-range parts
+// of the box are not written.
+__device__ __forceinline__ void tma_reduce_add_5d(const CUtensorMap *map, uint32_t src, int c0,
+                                                  int c1, int c2, int c3, int c4) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.5d.global.shared::cta.add.tile.bulk_group"
+      " [%0, {%2, %3, %4, %5, %6}], [%1];" ::"l"(reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+      : "memory");
+}
 __device__ __forceinline__ void bulk_commit_group() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
@@ -183,6 +194,40 @@ __device__ __forceinline__ void umma_ts_warp(uint32_t d_tmem, uint32_t a_tmem, u
       "setp.ne.b32 p, %4, 0;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Four single-CTA UMMAs under one elect.sync: the first accumulates when
+// acc0 != 0, the others always (the k-steps of one product).
+__device__ __forceinline__ void umma_ss_x4_warp(uint32_t d_tmem, const uint64_t (&a)[4],
+                                                const uint64_t (&b)[4], uint32_t idesc,
+                                                uint32_t acc0) {
+  asm volatile(
+      "{\n\t.reg .pred p, q, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %10, 0;\n\t"
+      "setp.eq.b32 q, %10, %10;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %5, %9, p;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %6, %9, q;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %7, %9, q;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %8, %9, q;\n\t}" ::"r"(d_tmem),
+      "l"(a[0]), "l"(a[1]), "l"(a[2]), "l"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]),
+      "r"(idesc), "r"(acc0)
+      : "memory");
+}
+__device__ __forceinline__ void umma_ts_x4_warp(uint32_t d_tmem, const uint32_t (&a)[4],
+                                                const uint64_t (&b)[4], uint32_t idesc,
+                                                uint32_t acc0) {
+  asm volatile(
+      "{\n\t.reg .pred p, q, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %10, 0;\n\t"
+      "setp.eq.b32 q, %10, %10;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %5, %9, p;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %6, %9, q;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%3], %7, %9, q;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %8, %9, q;\n\t}" ::"r"(d_tmem),
+      "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "l"(b[0]), "l"(b[1]), "l"(b[2]), "l"(b[3]),
+      "r"(idesc), "r"(acc0)
       : "memory");
 }
 __device__ __forceinline__ void umma_commit_warp(uint32_t bar) {
@@ -585,6 +630,18 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
       "r"(r[15])
       : "memory");
+}
+
+__device__ __forceinline__ void st_shared_f32(uint32_t addr, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ float4 ld_shared_v4f(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
 }
 
 // Four fp32 values added to global memory (16-byte aligned), no return.
