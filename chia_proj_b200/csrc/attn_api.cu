@@ -388,9 +388,9 @@ int decode_plan(const chia_attn_params_t *p, int sms, DecodePlan &pl) {
   return CHIA_OK;
 }
 
-template <int D, int RP, bool BF16>
+template <int D, int RP, bool BF16, int KIND>
 int launch_decode(const chia::DecodeArgs &a, dim3 grid, cudaStream_t s) {
-  auto kern = chia::decode_kernel<D, RP, BF16>;
+  auto kern = chia::decode_kernel<D, RP, BF16, KIND>;
   constexpr int smem = chia::decode_smem_bytes<D, RP>();
   static std::atomic<uint32_t> configured{0};
   int dev = 0;
@@ -406,9 +406,22 @@ int launch_decode(const chia::DecodeArgs &a, dim3 grid, cudaStream_t s) {
   return cudaGetLastError() == cudaSuccess ? CHIA_OK : CHIA_ERR_LAUNCH;
 }
 
+template <int D, int RP, bool BF16>
+int launch_decode_kind(const chia::DecodeArgs &a, dim3 grid, cudaStream_t s) {
+  switch (a.kind) {
+    case chia::KIND_SOFTMAX: return launch_decode<D, RP, BF16, chia::KIND_SOFTMAX>(a, grid, s);
+    case chia::KIND_SOFTCAP: return launch_decode<D, RP, BF16, chia::KIND_SOFTCAP>(a, grid, s);
+    case chia::KIND_ALIBI: return launch_decode<D, RP, BF16, chia::KIND_ALIBI>(a, grid, s);
+    case chia::KIND_SIGMOID: return launch_decode<D, RP, BF16, chia::KIND_SIGMOID>(a, grid, s);
+    case chia::KIND_RELU: return launch_decode<D, RP, BF16, chia::KIND_RELU>(a, grid, s);
+  }
+  return CHIA_ERR_INVALID_ARGUMENT;
+}
+
 template <int D, bool BF16>
 int launch_decode_rp(int rp, const chia::DecodeArgs &a, dim3 grid, cudaStream_t s) {
-  return rp == 16 ? launch_decode<D, 16, BF16>(a, grid, s) : launch_decode<D, 32, BF16>(a, grid, s);
+  return rp == 16 ? launch_decode_kind<D, 16, BF16>(a, grid, s)
+                  : launch_decode_kind<D, 32, BF16>(a, grid, s);
 }
 
 // ------------------------------------------------------------- backward

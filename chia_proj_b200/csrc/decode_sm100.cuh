@@ -25,8 +25,7 @@
 
 #include <cstdint>
 
-#include "mask_geom.cuh"
-#include "ptx.cuh"
+#include "fmha_sm100.cuh"
 
 namespace chia {
 
@@ -66,11 +65,12 @@ struct DecodeConfig {
 };
 
 struct RowC {  // per row of the CTA's head group
-  int64_t lo, hi;  // mask band of the row's query position
+  int32_t lo, hi;  // mask band of the row's query position (keys < 2^30)
   float k_mul;     // multiplies the raw score
   float k_bias;    // ALiBi slope * log2(e) (times (j - i)), or the sigmoid offset
   int32_t i;       // query position
   int32_t valid;   // row < rows
+  int32_t pad[2];
 };
 
 // RP: rows per K/V head padded to 16 or 32 (MMA row tiles of 16).
@@ -128,8 +128,10 @@ __device__ __forceinline__ uint32_t pack16(float lo, float hi) {
   return BF16 ? ptx::pack_bf16(lo, hi) : ptx::pack_f16(lo, hi);
 }
 
-// Grid: (splits, batch * heads_kv); 128 threads.
-template <int D, int RP, bool BF16>
+// Grid: (splits, batch * heads_kv); 128 threads. KIND: the score
+// modification and normaliser (compile time, so that the element loop has
+// no branches on it).
+template <int D, int RP, bool BF16, int KIND>
 __global__ void __launch_bounds__(128) decode_kernel(const DecodeArgs a) {
   using C = DecodeConfig<D>;
   constexpr int TK = C::TK, NST = C::NST, PITCH = C::PITCH;
@@ -144,6 +146,7 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeArgs a) {
   uint8_t *qsm = sm + BODY;                                       // [RP][PITCH] bf16 / f16
   RowC *rc = reinterpret_cast<RowC *>(sm + BODY + RP * PITCH);    // [RP]
   __shared__ int last_cta;
+  __shared__ int32_t band_lo_max, band_hi_min;  // over the valid rows
 
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int gid = lane >> 2, tig = lane & 3;
@@ -151,8 +154,8 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeArgs a) {
   const int kvh = blockIdx.y;  // b * heads_kv + head_kv
   const int b = kvh / a.heads_kv, hk = kvh % a.heads_kv;
   const MaskGeom &g = a.mask;
-  const int kind = a.kind;
-  const bool softmax = kind == 0 || kind == 1 || kind == 2;
+  constexpr int kind = KIND;
+  constexpr bool softmax = KIND == 0 || KIND == 1 || KIND == 2;
 
   // ---- per-row constants, Q rows (16-bit, padded rows zero) ----
   if (t < RP) {
@@ -161,7 +164,10 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeArgs a) {
     const int gi = r.valid ? t / a.sq : 0, qi = r.valid ? t % a.sq : 0;
     const int h = hk * a.group + gi;
     r.i = qi;
-    row_band(g, qi, r.lo, r.hi);
+    int64_t lo64, hi64;
+    row_band(g, qi, lo64, hi64);
+    r.lo = static_cast<int32_t>(lo64);
+    r.hi = static_cast<int32_t>(hi64 < 0 ? -1 : hi64);
     const float hp = a.head_param != nullptr ? a.head_param[h] : 1.0f;
     r.k_mul = a.score_scale * LOG2E;
     r.k_bias = 0.f;
@@ -174,6 +180,15 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeArgs a) {
     }
     if (kind == 4) r.k_mul = a.score_scale;              // ReLU
     rc[t] = r;
+  }
+  if (t == 0) {
+    band_lo_max = 0;
+    band_hi_min = 0x7fffffff;
+  }
+  __syncthreads();
+  if (t < a.rows) {  // the key range every valid row sees completely (dilation 1, no prefix)
+    atomicMax(&band_lo_max, rc[t].lo);
+    atomicMin(&band_hi_min, rc[t].hi);
   }
   for (int e = t; e < RP * (D / 8); e += C::THREADS) {  // 16-byte pieces of Q rows
     const int r = e / (D / 8), c = e % (D / 8);
@@ -230,10 +245,15 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeArgs a) {
   }
   const uint32_t qaddr = ptx::smem_u32(qsm);
 
+  Tracer trc(warp == 0 ? 0 : 1);
+  auto tr = [&](int tag) { if (lane == 0 && (warp == 0 || warp == 1)) trc(tag); };
+  tr(1);  // prologue issued
   for (int tile = 0; tile < ntiles; ++tile) {
     load_tile(tile + NST - 1);
     cp_async_wait<NST - 1>();  // tile `tile` has landed (this thread's copies)
+    tr(2);
     __syncthreads();           // ... and every thread's
+    tr(3);
     const uint32_t kst = ring + (tile % NST) * C::STAGE_BYTES + warp * 16 * PITCH;
     const uint32_t vst = kst + C::TILE_BYTES;
     // ---------------- S = Q K^T for this warp's 16 keys ----------------
@@ -258,7 +278,11 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeArgs a) {
       }
     }
     // ---------------- mod, mask, normaliser ----------------
-    const int64_t jw = k0 + static_cast<int64_t>(tile) * TK + warp * 16;
+    const int jw = static_cast<int>(k0) + tile * TK + warp * 16;
+    // every valid row sees these 16 keys: no element test (padded rows of the
+    // MMA are never stored, whatever their scores)
+    const bool full = g.dil == 1 && jw >= band_lo_max && jw + 15 <= band_hi_min &&
+                      jw + 16 <= k1;
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
 #pragma unroll
@@ -269,9 +293,12 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeArgs a) {
         for (int n = 0; n < 2; ++n)
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int64_t j = jw + n * 8 + 2 * tig + e;
+            const int j = jw + n * 8 + 2 * tig + e;
             const float sv = s[m][n][2 * h2 + e];
-            const bool vis = R.valid && j < k1 && visible(g, R.i, j, R.lo, R.hi);
+            const bool vis =
+                full || (R.valid && j < k1 &&
+                         (j < g.prefix ||
+                          (j >= R.lo && j <= R.hi && (g.dil == 1 || (R.i - j) % g.dil == 0))));
             float x;
             if (kind == 3) {  // sigmoid(s * scale + bias)
               const float ex = ptx::ex2(fminf(fmaf(sv, R.k_mul, R.k_bias), 126.f));
@@ -307,14 +334,17 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeArgs a) {
             }
           l_run[m][h2] = l_run[m][h2] * alpha + sum;  // this lane's keys only
           m_run[m][h2] = m_new;
+          if (__any_sync(0xffffffffu, alpha != 1.0f)) {  // the maximum grew somewhere
 #pragma unroll
-          for (int n = 0; n < NT; ++n) {
-            o[m][n][2 * h2] *= alpha;
-            o[m][n][2 * h2 + 1] *= alpha;
+            for (int n = 0; n < NT; ++n) {
+              o[m][n][2 * h2] *= alpha;
+              o[m][n][2 * h2 + 1] *= alpha;
+            }
           }
         }
       }
     }
+    tr(4);  // scores and softmax done
     // ---------------- O += P V ----------------
 #pragma unroll
     for (int m = 0; m < MT; ++m) {
@@ -333,10 +363,12 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeArgs a) {
         mma16816<BF16>(o[m][2 * n2 + 1], pa, b2, b3);
       }
     }
+    tr(5);  // P V done
     __syncthreads();  // the stage is refilled by the next iteration's load
   }
   cp_async_wait<0>();
   __syncthreads();
+  tr(6);  // main loop done
 
   // ---------------- merge the four warps (shared memory) ----------------
   float *mo = reinterpret_cast<float *>(sm);            // [4][RP][D]
@@ -385,6 +417,7 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeArgs a) {
   __syncthreads();
   if (t == 0) last_cta = atomicAdd(a.tickets + kvh, 1) == a.splits - 1;
   __syncthreads();
+  tr(7);  // partial result written
   if (!last_cta) return;
   __threadfence();
 
@@ -460,6 +493,7 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeArgs a) {
           L > 0.f ? (m_sm[r] + __log2f(L)) * LN2 : -INFINITY;
     }
   }
+  tr(8);  // merged
   if (t == 0) a.tickets[kvh] = 0;  // ready for the next launch
 }
 
