@@ -681,11 +681,15 @@ int chia_attn_abi_version(void) { return CHIA_ATTN_ABI_VERSION; }
 
 #ifdef CHIA_TRACE
 // Trace builds only (not part of the public ABI): copy the timeline buffer
-// of the last traced launch to host memory; returns bytes copied.
+// of the last traced launch to host memory and clear it; returns bytes copied.
 __attribute__((visibility("default"))) long chia_attn_trace_read(void *dst, long bytes) {
   const long n = bytes < static_cast<long>(sizeof(chia::g_chia_trace))
                      ? bytes : static_cast<long>(sizeof(chia::g_chia_trace));
   if (cudaMemcpyFromSymbol(dst, chia::g_chia_trace, n) != cudaSuccess) return -1;
+  void *sym = nullptr;
+  if (cudaGetSymbolAddress(&sym, chia::g_chia_trace) != cudaSuccess ||
+      cudaMemset(sym, 0, sizeof(chia::g_chia_trace)) != cudaSuccess)
+    return -1;
   return n;
 }
 #endif

@@ -159,6 +159,127 @@ __device__ __forceinline__ bool reverse_tiles(const KernelArgs &a, const UnitInf
   return KIND == KIND_ALIBI && a.head_param[U.h] > 0.f;
 }
 
+// ---- masked tiles of the softmax kinds (64 columns per thread) ----
+// A tile that is not wholly visible is classified per 32-column chunk,
+// uniformly over the warp: a chunk every row of the warp sees completely
+// takes the unmasked code, a chunk no row sees is skipped (P = 0, no
+// exponentials), only the rest applies a per-column visibility bit. The
+// warp's 32 rows are 32 consecutive queries, so on a causal or banded
+// diagonal tile most chunks are one or the other.
+
+// Visibility of columns col0 .. col0+31 (relative to RowMask's column 0)
+// for this thread's row, one bit per column: the band [c_lo, c_lo + span]
+// thinned to the row's dilation residue, or'ed with the always-visible
+// prefix. dil_pat has a bit at every multiple of the dilation below 32.
+__device__ __forceinline__ uint32_t visible_bits(const RowMask &rm, int col0, uint32_t dil_pat) {
+  uint32_t w = 0u;
+  const int64_t lo = static_cast<int64_t>(rm.c_lo) - col0;
+  const int64_t hi = lo + rm.span;
+  if (lo <= 31 && hi >= 0) {
+    const int l = lo < 0 ? 0 : static_cast<int>(lo);
+    const int h = hi > 31 ? 31 : static_cast<int>(hi);
+    w = (0xFFFFFFFFu >> (31 - h)) & (0xFFFFFFFFu << l);
+  }
+  if (rm.dil > 1) {
+    // visible: columns col0 + p, p = (i - key of column col0) mod dil (+ k dil)
+    int p0 = (rm.i_rel - col0) % rm.dil;
+    if (p0 < 0) p0 += rm.dil;
+    w &= p0 < 32 ? dil_pat << p0 : 0u;
+  }
+  const int n = rm.c_pre - col0;
+  const uint32_t pre = n <= 0 ? 0u : (n >= 32 ? 0xFFFFFFFFu : (1u << n) - 1u);
+  return w | pre;
+}
+
+// Pass 1 of one chunk, in place: score -> log2-domain logit (columns whose
+// bit in vis is clear -> -inf when MASK); returns the chunk maximum.
+template <int KIND, bool MASK>
+__device__ __forceinline__ float logit_chunk(uint32_t (&x)[32], int col0, const EpiConsts &k,
+                                             uint32_t vis) {
+  const uint64_t K2 = ptx::f2(k.k_mul, k.k_mul);
+  const uint64_t CAP2 = ptx::f2(k.k_cap, k.k_cap);
+  const uint64_t KB2 = ptx::f2(k.k_bias, k.k_bias);
+  const uint64_t REL2 = ptx::f2(k.rel0 + static_cast<float>(col0), k.rel0 + static_cast<float>(col0 + 1));
+  float mc = -INFINITY;
+#pragma unroll
+  for (int e = 0; e < 32; e += 2) {
+    uint64_t x2 = ptx::mul2(ptx::f2(__uint_as_float(x[e]), __uint_as_float(x[e + 1])), K2);
+    if (KIND == KIND_SOFTCAP) {
+      float a, b;
+      ptx::f2_split(x2, a, b);
+      x2 = ptx::mul2(ptx::f2(ptx::tanh_fast(a), ptx::tanh_fast(b)), CAP2);
+    } else if (KIND == KIND_ALIBI) {
+      // bias = slope * (j - i): (j - i) is formed exactly before scaling
+      const uint64_t rel = ptx::add2(REL2, ptx::f2(static_cast<float>(e), static_cast<float>(e)));
+      x2 = ptx::fma2(KB2, rel, x2);
+    }
+    float a, b;
+    ptx::f2_split(x2, a, b);
+    if (MASK) {
+      if (!((vis >> e) & 1u)) a = -INFINITY;
+      if (!((vis >> (e + 1)) & 1u)) b = -INFINITY;
+    }
+    mc = ptx::max3(mc, a, b);
+    x[e] = __float_as_uint(a);
+    x[e + 1] = __float_as_uint(b);
+  }
+  return mc;
+}
+
+// Pass 1 of a masked tile on this thread's 64 columns; bit c of `skip` is
+// set for a chunk no row of the warp sees (its logits are left unwritten).
+template <int KIND>
+__device__ __forceinline__ float softmax_pass1_masked(uint32_t (&sr)[2][32], const EpiConsts &k,
+                                                      const RowMask &rm, uint32_t dil_pat,
+                                                      uint32_t &skip) {
+  float m = -INFINITY;
+  skip = 0u;
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    const uint32_t vis = visible_bits(rm, c * 32, dil_pat);
+    if (__all_sync(0xffffffffu, vis == 0u)) {
+      skip |= 1u << c;
+    } else if (__all_sync(0xffffffffu, vis == 0xFFFFFFFFu)) {
+      m = fmaxf(m, logit_chunk<KIND, false>(sr[c], c * 32, k, 0u));
+    } else {
+      m = fmaxf(m, logit_chunk<KIND, true>(sr[c], c * 32, k, vis));
+    }
+  }
+  return m;
+}
+
+// Pass 2 with skipped chunks: P = 2^(x - m) of the chunks not in `skip`, 0 for
+// the others, packed over the first 32 of these columns; returns the row sum.
+template <bool BF16>
+__device__ __forceinline__ float softmax_pass2_skip(const uint32_t (&sr)[2][32], float m,
+                                                    uint32_t skip, uint32_t tP) {
+  const uint64_t NM2 = ptx::f2(-m, -m);
+  uint64_t acc[2] = {ptx::f2(0.f, 0.f), ptx::f2(0.f, 0.f)};
+  uint32_t pk[32];
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    if ((skip >> c) & 1u) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) pk[c * 16 + e] = 0u;
+      continue;
+    }
+#pragma unroll
+    for (int e = 0; e < 32; e += 2) {
+      float a, b;
+      ptx::f2_split(ptx::add2(ptx::f2(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])), NM2),
+                    a, b);
+      const float p0 = ptx::ex2(a), p1 = ptx::ex2(b);
+      acc[c] = ptx::add2(acc[c], ptx::f2(p0, p1));
+      pk[c * 16 + e / 2] = pack2<BF16>(p0, p1);
+    }
+  }
+  ptx::tmem_st32(tP, pk);
+  float s0, s1, s2, s3;
+  ptx::f2_split(acc[0], s0, s1);
+  ptx::f2_split(acc[1], s2, s3);
+  return (s0 + s1) + (s2 + s3);
+}
+
 // Bounded wait on a local barrier that may receive arrivals from the other CTA.
 __device__ __forceinline__ bool bounded_wait_cl(const WaitCtx &c, uint32_t bar, uint32_t parity,
                                                 bool honour_abort = true) {
@@ -522,6 +643,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
     const uint32_t tO = tmem_base + lane_off + C::TMEM_O + half * 64;
     const int prefix = static_cast<int>(g.prefix);
     const int dil = static_cast<int>(g.dil);
+    uint32_t dil_pat = 0u;  // a bit at every multiple of the dilation below 32
+    for (int p = 0; p < 32; p += dil) dil_pat |= 1u << p;
     const uint32_t pfull0 = lbar(C::BAR_PFULL), oempty = lbar(C::BAR_OEMPTY);
     float *xch = reinterpret_cast<float *>(smem + C::OFF_XCH);
     uint32_t xcnt = 0;
@@ -622,12 +745,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
           const PSinkTmem sink{tS};  // P of these 64 keys -> first 32 of these columns
           if (SOFTMAX) {
             float mx;
+            uint32_t skip = 0u;  // chunks of a masked tile no row of this warp sees
             if (mode == 0)
-              mx = softmax_pass1<KIND, 0>(sr, kc, rm);
-            else if (mode == 1)
-              mx = softmax_pass1<KIND, 1>(sr, kc, rm);
+              mx = softmax_pass1<KIND, 0, 2>(sr, kc, rm);
             else
-              mx = softmax_pass1<KIND, 2>(sr, kc, rm);
+              mx = softmax_pass1_masked<KIND>(sr, kc, rm, dil_pat, skip);
+            auto pass2 = [&](float m) -> float {
+              return skip == 0u ? softmax_pass2<BF16>(sr, m, sink)
+                                : softmax_pass2_skip<BF16>(sr, m, skip, tS);
+            };
             // The row maximum of the whole tile needs the other half's. After
             // the first tile, P is computed optimistically against the running
             // maximum, which stays exact unless the maximum grew by more than
@@ -635,7 +761,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
             // afterwards, when it has long been published.
             publish(mx);
             float lsum = 0.f;
-            if (!first_mine) lsum = softmax_pass2<BF16>(sr, m_run == -INFINITY ? 0.f : m_run, sink);
+            if (!first_mine) lsum = pass2(m_run == -INFINITY ? 0.f : m_run);
             float mx_other;
             if (!collect(mx_other)) { ok = false; break; }
             mx = fmaxf(mx, mx_other);  // row maximum over the whole tile
@@ -660,7 +786,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
                 rescale_rows<64>(tO, alpha);
               }
               // (re)compute P against the new maximum; P is not yet signalled
-              lsum = softmax_pass2<BF16>(sr, m_run == -INFINITY ? 0.f : m_run, sink);
+              lsum = pass2(m_run == -INFINITY ? 0.f : m_run);
             }
             l_run += lsum;
           } else {

@@ -344,10 +344,12 @@ __device__ __forceinline__ float softmax_pass2(uint32_t (&sr)[NC][32], float m, 
 
 // Non-softmax kinds: P = relu(s * scale) or sigmoid(s * scale + bias),
 // masked, packed and handed to the P sink.
-// Sigmoid is 1 / (1 + 2^t): 2^t on the MUFU, the reciprocal on the FMA pipe
-// (initial guess from the exponent-field complement 0x7EF311C7 - bits(y),
-// then two Newton steps r <- r (2 - y r); relative error about 2e-4, below
-// the 2^-9 rounding of the 16-bit P).
+// Sigmoid is 1 / (1 + 2^t): 2^t on the MUFU, the reciprocal on the FMA pipe:
+// an initial guess r0 = as_float(0x7EF311C2 - bits(y)) and two Newton steps
+// r <- r (2 - y r). The constant minimises the largest relative error of r0
+// over all y (0.0505; the search is recip_seed.py beside this file), so after
+// two steps the error is about 0.0505^4 = 6.5e-6, far below the 2^-9 rounding
+// of the 16-bit P. y is negated here (-(1 + 2^t)), hence 0xFEF311C2 - bits.
 // One 32-column chunk (src, columns col0..col0+31 of the tile) of the
 // pointwise kinds, as 16 packed pairs into pk[off .. off+15].
 template <int KIND, int MODE, bool BF16>
@@ -378,8 +380,8 @@ __device__ __forceinline__ void pointwise_chunk(const uint32_t (&src)[32], int c
       const uint64_t ny = ptx::fma2(e2, NEG1, NEG1);  // -(1 + 2^t)
       float y0, y1;
       ptx::f2_split(ny, y0, y1);
-      uint64_t r = ptx::f2(__uint_as_float(0xFEF311C7u - __float_as_uint(y0)),
-                           __uint_as_float(0xFEF311C7u - __float_as_uint(y1)));
+      uint64_t r = ptx::f2(__uint_as_float(0xFEF311C2u - __float_as_uint(y0)),
+                           __uint_as_float(0xFEF311C2u - __float_as_uint(y1)));
       r = ptx::mul2(r, ptx::fma2(ny, r, TWO2));
       r = ptx::mul2(r, ptx::fma2(ny, r, TWO2));
       ptx::f2_split(r, a, b);

@@ -17,8 +17,10 @@ Numerics: q.k and P.V run on the tensor cores with fp32 accumulation; the
 score modification, mask and normaliser run in fp32; P is rounded to the
 input dtype before P.V, as the reference's ``p.to(DT) @ v`` does
 (``extra_bench.py:45``). fp32 inputs are accepted for signature
-compatibility and computed in bf16 (the tensor-core input type), output
-returned in fp32.
+and computed on the tensor cores with 16-bit operands and fp32 accumulation:
+fp16 operands (a 10-bit mantissa, the precision of a TF32 MMA) when every
+input element and every score fits fp16's range, else bf16 operands;
+``compute_dtype`` chooses explicitly. The output is returned in fp32.
 """
 
 from __future__ import annotations
@@ -177,6 +179,26 @@ def _prep(x: torch.Tensor) -> torch.Tensor:
     return x
 
 
+_FP16_MAX = 65504.0
+
+
+def _fp32_operand_dtype(q, k, v, norm: str, scale) -> torch.dtype:
+    """Operand type for fp32 inputs: fp16 when nothing the kernel rounds to
+    16 bits can leave fp16's range, else bf16. The inputs must fit; so must P,
+    which is at most 1 for softmax and sigmoid and at most
+    max|q| max|k| D scale for ReLU (the output scale is applied after P.V)."""
+    amax = torch.stack([torch.linalg.vector_norm(t.detach(), float("inf"))
+                        for t in (q, k, v)]).cpu()
+    if not bool(torch.isfinite(amax).all()) or float(amax.max()) > _FP16_MAX:
+        return torch.bfloat16
+    if norm == "relu":
+        D = q.shape[-1]
+        sc = abs(scale) if scale is not None else 1.0 / math.sqrt(D)
+        if float(amax[0]) * float(amax[1]) * D * sc > _FP16_MAX:
+            return torch.bfloat16
+    return torch.float16
+
+
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
               norm: str = "softmax", mod: str = "none", mask: Mask = CAUSAL,
               scale: Optional[float] = None, softcap: float = 30.0,
@@ -184,11 +206,16 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
               sig_bias: float = 0.0, out_scale: float = 1.0,
               out: Optional[torch.Tensor] = None, schedule: str = "dynamic",
               cu_seqlens=None, return_lse: bool = False, wait_limit_ns: int = 0,
-              split_kv: Optional[bool] = None):
+              split_kv: Optional[bool] = None,
+              compute_dtype: Optional[torch.dtype] = None):
     """Generic forward attention: ``norm(mask(mod(q.k * scale))) @ v``.
 
-    ``q, k, v``: CUDA tensors ``[B, H, S, D]`` (bf16 / fp16; fp32 computed as
-    bf16), ``D`` in {64, 128}. ``k`` and ``v`` may have ``H_kv`` heads with
+    ``q, k, v``: CUDA tensors ``[B, H, S, D]`` (bf16 / fp16 / fp32), ``D`` in
+    {64, 128}. fp32 inputs are computed with 16-bit tensor-core operands and
+    fp32 accumulation, and the output is fp32: ``compute_dtype`` (fp16 or
+    bf16) names the operand type; ``None`` takes fp16 (10 mantissa bits, as
+    a TF32 MMA keeps) when the inputs and the largest possible score fit its
+    range, else bf16. ``k`` and ``v`` may have ``H_kv`` heads with
     ``H % H_kv == 0`` (grouped-query attention: query head ``h`` reads K/V
     head ``h // (H // H_kv)``). ``head_param``: ALiBi slopes (``mod="alibi"``)
     or logit multipliers (``mod="temp"``), one per head. ``schedule``:
@@ -247,9 +274,15 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
         raise ValueError("wait_limit_ns must be >= 0")
     in_dtype = q.dtype
     if in_dtype == torch.float32:
-        q, k, v = q.to(torch.bfloat16), k.to(torch.bfloat16), v.to(torch.bfloat16)
+        cdt = (compute_dtype if compute_dtype is not None
+               else _fp32_operand_dtype(q, k, v, norm, scale))
+        if cdt not in (torch.float16, torch.bfloat16):
+            raise ValueError("compute_dtype must be torch.float16 or torch.bfloat16")
+        q, k, v = q.to(cdt), k.to(cdt), v.to(cdt)
     elif in_dtype not in (torch.bfloat16, torch.float16):
         raise ValueError(f"dtype {in_dtype} unsupported")
+    elif compute_dtype is not None and compute_dtype != in_dtype:
+        raise ValueError("compute_dtype applies to fp32 inputs only")
     q, k, v = _prep(q), _prep(k), _prep(v)
     dev = q.device
     if out is None or in_dtype == torch.float32:

@@ -150,12 +150,76 @@ def test_strided_inputs(cuda):
 
 
 def test_fp32_inputs_accepted(cuda):
-    """Config-1 shape in fp32 (computed in bf16 on the tensor cores)."""
+    """Config-1 shape in fp32: fp16 operands (the mantissa of a TF32 MMA) with
+    fp32 accumulation, an order of magnitude closer to the fp32 reference than
+    bf16 operands, which remain available through ``compute_dtype``."""
     q, k, v = gen(1, 8, 512, 64, torch.float32, seed=1)
     ref = oracle.run_op("softcap_gemma2", q, k, v, cap=50.0, causal=False)
     out = run("softcap_gemma2", q, k, v, cap=50.0, causal=False)
     assert out.dtype == torch.float32
     check(out, ref, "fp32 config 1")
+    dev = torch.device("cuda", 0)
+    qd, kd, vd = q.to(dev), k.to(dev), v.to(dev)
+    kw = dict(mod="softcap", softcap=50.0, mask=cp.FULL)
+    o16 = cp.attention(qd, kd, vd, **kw).cpu()
+    obf = cp.attention(qd, kd, vd, compute_dtype=torch.bfloat16, **kw).cpu()
+    e16, ebf = (o16 - ref).abs(), (obf - ref).abs()
+    assert torch.equal(o16, out.cpu())
+    assert e16.max() < 2e-3 and e16.mean() < 2e-4, (e16.max(), e16.mean())
+    assert e16.max() < 0.25 * ebf.max() and e16.mean() < 0.25 * ebf.mean()
+
+
+def test_fp32_inputs_outside_fp16_range_use_bf16(cuda):
+    """Inputs (or ReLU scores) that fp16 cannot hold fall back to bf16 operands."""
+    q, k, v = gen(1, 2, 256, 64, torch.float32, seed=3)
+    dev = torch.device("cuda", 0)
+    big = v.clone()
+    big[0, 0, 0, 0] = 1.0e5  # row 0 sees key 0 alone: its output is this value
+    ref = oracle.run_op("bias_dilated", q, k, big, dilation=1)
+    out = cp.attention(q.to(dev), k.to(dev), big.to(dev))
+    assert torch.isfinite(out).all()
+    forced = cp.attention(q.to(dev), k.to(dev), big.to(dev), compute_dtype=torch.bfloat16)
+    assert torch.equal(out, forced)
+    # ReLU: P = relu(s * scale) reaches 8 * 8 * 64 / 8 = 512 here but 5e5 with
+    # 100-fold inputs, which fp16 cannot hold
+    q2, k2 = q * 100.0, k * 100.0
+    o_auto = cp.attention(q2.to(dev), k2.to(dev), v.to(dev), norm="relu", mask=cp.FULL)
+    o_bf = cp.attention(q2.to(dev), k2.to(dev), v.to(dev), norm="relu", mask=cp.FULL,
+                        compute_dtype=torch.bfloat16)
+    assert torch.equal(o_auto, o_bf)
+    with pytest.raises(ValueError):
+        cp.attention(q2.to(dev).half(), k2.to(dev).half(), v.to(dev).half(),
+                     compute_dtype=torch.bfloat16)
+    check(out, ref, "fp32, element out of fp16 range")
+
+
+def _eager_dt(op, q, k, v):
+    """The reference's eager operator evaluated in the inputs' 16-bit type,
+    as its own benchmark harness runs it (``extra_bench.py:38-45``): scores
+    rounded to DT, the normaliser in fp32, ``p.to(DT) @ v``. Sigmoid and ReLU
+    at the reference's defaults (causal, no bias, no output scale)."""
+    S, D = q.shape[-2], q.shape[-1]
+    s = (q @ k.transpose(-2, -1)) * (1.0 / math.sqrt(D))
+    i = torch.arange(S).view(-1, 1)
+    j = torch.arange(S).view(1, -1)
+    ok = (j <= i).float()
+    p = torch.sigmoid(s.float()) * ok if op == "sigmoid_attn" else torch.relu(s.float()) * ok
+    return (p.to(q.dtype) @ v).float()
+
+
+@pytest.mark.parametrize("op", ["sigmoid_attn", "relu_attn"])
+def test_unnormalised_defaults_no_worse_than_bf16_eager(cuda, op):
+    """At the reference's default parameters sigmoid and ReLU outputs grow like
+    sqrt(S), so ``check`` scales its absolute bounds by max|ref|. This measures
+    what that allowance is for: the reference's own eager computation in bf16
+    misses its fp32 result by at least as much as the kernel does."""
+    q, k, v = gen(1, 4, 512, 128, torch.bfloat16, seed=21)
+    ref = oracle.run_op(op, q, k, v)
+    out = run(op, q, k, v).float().cpu()
+    eager = _eager_dt(op, q, k, v)
+    e_k, e_e = (out - ref).abs(), (eager - ref).abs()
+    assert e_k.max() <= 1.1 * e_e.max(), (e_k.max(), e_e.max())
+    assert e_k.mean() <= 1.1 * e_e.mean(), (e_k.mean(), e_e.mean())
 
 
 def test_preallocated_output(cuda):
