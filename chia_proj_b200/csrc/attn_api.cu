@@ -222,7 +222,7 @@ template <bool BF16, int KIND, bool MASKED, bool SEG>
 int launch_pair(const CUtensorMap &mq, const CUtensorMap &mkh, const CUtensorMap &mvh,
                 const CUtensorMap &mo, const chia::KernelArgs &a, int64_t nunits,
                 cudaStream_t stream) {
-  using Cfg = chia::Fmha2Config<128>;
+  using Cfg = chia::Fmha2Config<128, chia::fmha2_parts(KIND)>;
   auto kern = chia::fmha2_fwd_kernel<128, BF16, KIND, MASKED, SEG>;
   static std::atomic<uint32_t> configured{0};
   static std::atomic<int> max_pairs[32];

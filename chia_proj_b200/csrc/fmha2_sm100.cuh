@@ -13,11 +13,11 @@
 //
 // Per CTA, tensor memory (512 columns x 128 lanes):
 //   cols [0,384)  three S/P buffers of 128 columns,  cols [384,512) O
-// Tile t uses buffer t % 3. Its softmax output P (16-bit pairs) overwrites
-// columns [0,32) (keys 0-63) and [64,96) (keys 64-127) of that buffer, each
-// half inside the S columns of the warpgroup that wrote it, and is read back
-// by the TS-UMMA. With three buffers the MMA warp keeps S up to three tiles
-// ahead of the softmax warpgroups:
+// Tile t uses buffer t % 3. Its softmax output P (16-bit pairs) of the COLS
+// keys of column part p overwrites columns [p COLS, p COLS + COLS/2) of that
+// buffer, inside the S columns of the warpgroup that wrote it, and is read
+// back by the TS-UMMA. With three buffers the MMA warp keeps S up to three
+// tiles ahead of the softmax warpgroups:
 //   per tile i:  once P(t_i) is ready, O += P(t_i) V(t_i), then S(t_{i+3})
 // into the buffer P(t_i) just left (UMMAs of one thread run in order).
 // K and V halves of a tile share one ring stage (one wait, one release).
@@ -27,13 +27,14 @@
 // there, and the load thread stores it with TMA before it loads the Q of
 // the unit two ahead into the same buffer.
 //
-// Warps per CTA: 0-7 two softmax warpgroups; warp w owns TMEM lanes (query
-// rows) 32 (w % 4) .. +31 and key columns 64 (w / 4) .. +63 of every tile, so
-// each thread transforms half a row. Softmax kinds combine the two halves'
-// row maxima through shared memory once per tile (64-thread named barrier per
-// lane quadrant) and the row sums once per unit; each warpgroup rescales and
-// stores its own 64 columns of O. Warp 8 issues MMAs (the even CTA's lane 0;
-// both CTAs' warp 8 allocate TMEM), warp 9 loads.
+// Warps per CTA: 4 NP softmax warps in NP warpgroups (NP = 2 for the softmax
+// kinds, 4 for sigmoid and ReLU); warp w owns TMEM lanes (query rows)
+// 32 (w % 4) .. +31 and key columns COLS (w / 4) .. +COLS-1 of every tile
+// (COLS = 128 / NP), so each thread transforms 1/NP of a row. Softmax kinds
+// combine the parts' row maxima through shared memory once per tile and the
+// row sums once per unit; each warpgroup rescales and stores its own COLS
+// columns of O. Warp 4 NP issues MMAs (the even CTA's lane 0; both CTAs'
+// warp 4 NP allocate TMEM), warp 4 NP + 1 loads.
 // Barriers that collect both CTAs live in the even CTA; the even CTA's
 // commits are multicast to both. The (dynamic) unit index and its key-tile
 // count are broadcast by the even CTA's load thread into both CTAs' unit
@@ -44,11 +45,28 @@
 
 namespace chia {
 
-template <int D>
+// Column parts per row (softmax warpgroups): four for sigmoid, whose
+// per-score work (exponential, reciprocal seed, two Newton steps) is long
+// enough that four warps per SM sub-partition hide its latencies better (3%
+// in an A/B run on one GPU); two for ReLU (1.5% slower with four) and for the
+// softmax kinds, which exchange row maxima between the parts every tile.
+__host__ __device__ constexpr int fmha2_parts(int kind) {
+  return kind == KIND_SIGMOID ? 4 : 2;
+}
+
+template <int D, int NP_ = 2>
 struct Fmha2Config {
   static_assert(D == 128, "the 2-SM kernel is specialised for head_dim 128");
   static constexpr int BM = 128;  // query rows per CTA
   static constexpr int BN = 128;  // keys per tile
+  // softmax warpgroups = column parts of a row: each thread owns COLS keys
+  // (CH chunks of 32) of its row in every tile
+  static constexpr int NP = NP_;
+  static constexpr int COLS = BN / NP;
+  static constexpr int CH = COLS / 32;
+  static_assert(NP == 2 || NP == 4, "two or four column parts");
+  // the row-maximum / row-sum exchange is written for two parts
+  static constexpr bool EXCHANGE = NP == 2;
   static constexpr int Q_BYTES = BM * D * 2;          // 32 KB, two 128-byte chunks
   static constexpr int Q_CHUNK = BM * 128;            // 16 KB
   static constexpr int KH_ROWS = BN / 2;              // keys per CTA per K tile
@@ -90,7 +108,7 @@ struct Fmha2Config {
   // tmem base, abort flag, unit ring [2], key tiles of the ring's units [2]
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   // row-max / row-sum exchange between the two softmax warpgroups:
-  // float [2 parity][2 column half][128 rows]
+  // float [2 parity][2 column part][128 rows]
   static constexpr int OFF_XCH = OFF_MISC + 32;
   // unit queue: 4 UnitSlot entries
   static constexpr int OFF_UQ = OFF_XCH + 2 * 2 * 128 * 4;
@@ -99,10 +117,10 @@ struct Fmha2Config {
   // without static shared memory starts 1024-byte aligned (checked at run
   // time), and the second Q buffer needs the room.
   static constexpr int SMEM_ALLOC = SMEM_BYTES;
-  static constexpr int THREADS = 320;
-  static constexpr int SOFTMAX_WARPS = 8;
-  static constexpr int MMA_WARP = 8;
-  static constexpr int LOAD_WARP = 9;
+  static constexpr int SOFTMAX_WARPS = 4 * NP;
+  static constexpr int MMA_WARP = SOFTMAX_WARPS;
+  static constexpr int LOAD_WARP = SOFTMAX_WARPS + 1;
+  static constexpr int THREADS = 32 * (SOFTMAX_WARPS + 2);
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t TMEM_O = 384;
   static constexpr int UNIT_CONSUMERS = 2;  // of the ring: the MMA warp, the odd CTA's loader
@@ -226,38 +244,44 @@ __device__ __forceinline__ float logit_chunk(uint32_t (&x)[32], int col0, const 
   return mc;
 }
 
-// Pass 1 of a masked tile on this thread's 64 columns; bit c of `skip` is
-// set for a chunk no row of the warp sees (its logits are left unwritten).
-template <int KIND>
-__device__ __forceinline__ float softmax_pass1_masked(uint32_t (&sr)[2][32], const EpiConsts &k,
-                                                      const RowMask &rm, uint32_t dil_pat,
-                                                      uint32_t &skip) {
+// Pass 1 on this thread's CH chunks: scores -> logits in place; returns the
+// maximum. MASK_TILE: the tile is not wholly visible, so each chunk is
+// classified first; bit c of `skip` is set for a chunk no row of the warp
+// sees (its logits are left unwritten).
+template <int KIND, int CH, bool MASK_TILE>
+__device__ __forceinline__ float softmax_pass1_cols(uint32_t (&sr)[CH][32], const EpiConsts &k,
+                                                    const RowMask &rm, uint32_t dil_pat,
+                                                    uint32_t &skip) {
   float m = -INFINITY;
   skip = 0u;
 #pragma unroll
-  for (int c = 0; c < 2; ++c) {
-    const uint32_t vis = visible_bits(rm, c * 32, dil_pat);
-    if (__all_sync(0xffffffffu, vis == 0u)) {
-      skip |= 1u << c;
-    } else if (__all_sync(0xffffffffu, vis == 0xFFFFFFFFu)) {
-      m = fmaxf(m, logit_chunk<KIND, false>(sr[c], c * 32, k, 0u));
-    } else {
-      m = fmaxf(m, logit_chunk<KIND, true>(sr[c], c * 32, k, vis));
+  for (int c = 0; c < CH; ++c) {
+    if (MASK_TILE) {
+      const uint32_t vis = visible_bits(rm, c * 32, dil_pat);
+      if (__all_sync(0xffffffffu, vis == 0u)) {
+        skip |= 1u << c;
+        continue;
+      }
+      if (!__all_sync(0xffffffffu, vis == 0xFFFFFFFFu)) {
+        m = fmaxf(m, logit_chunk<KIND, true>(sr[c], c * 32, k, vis));
+        continue;
+      }
     }
+    m = fmaxf(m, logit_chunk<KIND, false>(sr[c], c * 32, k, 0u));
   }
   return m;
 }
 
-// Pass 2 with skipped chunks: P = 2^(x - m) of the chunks not in `skip`, 0 for
-// the others, packed over the first 32 of these columns; returns the row sum.
-template <bool BF16>
-__device__ __forceinline__ float softmax_pass2_skip(const uint32_t (&sr)[2][32], float m,
+// Pass 2: P = 2^(x - m) of the chunks not in `skip`, 0 for the others,
+// packed over the first CH * 16 of these columns; returns the row sum.
+template <bool BF16, int CH>
+__device__ __forceinline__ float softmax_pass2_cols(const uint32_t (&sr)[CH][32], float m,
                                                     uint32_t skip, uint32_t tP) {
   const uint64_t NM2 = ptx::f2(-m, -m);
   uint64_t acc[2] = {ptx::f2(0.f, 0.f), ptx::f2(0.f, 0.f)};
-  uint32_t pk[32];
+  uint32_t pk[CH * 16];
 #pragma unroll
-  for (int c = 0; c < 2; ++c) {
+  for (int c = 0; c < CH; ++c) {
     if ((skip >> c) & 1u) {
 #pragma unroll
       for (int e = 0; e < 16; ++e) pk[c * 16 + e] = 0u;
@@ -269,15 +293,52 @@ __device__ __forceinline__ float softmax_pass2_skip(const uint32_t (&sr)[2][32],
       ptx::f2_split(ptx::add2(ptx::f2(__uint_as_float(sr[c][e]), __uint_as_float(sr[c][e + 1])), NM2),
                     a, b);
       const float p0 = ptx::ex2(a), p1 = ptx::ex2(b);
-      acc[c] = ptx::add2(acc[c], ptx::f2(p0, p1));
+      // one accumulator per chunk; a single chunk alternates two
+      const int ai = CH == 2 ? c : (e >> 1) & 1;
+      acc[ai] = ptx::add2(acc[ai], ptx::f2(p0, p1));
       pk[c * 16 + e / 2] = pack2<BF16>(p0, p1);
     }
   }
-  ptx::tmem_st32(tP, pk);
+  if constexpr (CH == 2)
+    ptx::tmem_st32(tP, pk);
+  else
+    ptx::tmem_st16(tP, pk);
   float s0, s1, s2, s3;
   ptx::f2_split(acc[0], s0, s1);
   ptx::f2_split(acc[1], s2, s3);
   return (s0 + s1) + (s2 + s3);
+}
+
+// Pointwise kinds on this thread's CH chunks of a TMEM S tile: P (CH * 32
+// keys) goes back over the first CH * 16 columns.
+template <int KIND, int MODE, bool BF16, int CH>
+__device__ __forceinline__ void pointwise_tmem_cols(uint32_t tS, const EpiConsts &k,
+                                                    const RowMask &rm) {
+  if constexpr (CH == 2) {
+    pointwise_tmem64<KIND, MODE, BF16>(tS, k, rm);
+  } else {
+    uint32_t s0[32], pk[32];
+    ptx::tmem_ld32(tS, s0);
+    ptx::tmem_wait_ld();
+    ptx::reg_fence(s0);
+    pointwise_chunk<KIND, MODE, BF16>(s0, 0, k, rm, pk, 0);
+    uint32_t p16[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) p16[e] = pk[e];
+    ptx::tmem_st16(tS, p16);
+  }
+}
+
+// P = 0 over the first CH * 16 columns at tS.
+template <int CH>
+__device__ __forceinline__ void tmem_zero_cols(uint32_t tS) {
+  uint32_t z[CH * 16];
+#pragma unroll
+  for (int e = 0; e < CH * 16; ++e) z[e] = 0u;
+  if constexpr (CH == 2)
+    ptx::tmem_st32(tS, z);
+  else
+    ptx::tmem_st16(tS, z);
 }
 
 // Bounded wait on a local barrier that may receive arrivals from the other CTA.
@@ -309,12 +370,12 @@ __device__ __forceinline__ bool bounded_wait_cl(const WaitCtx &c, uint32_t bar, 
 // checks: no window, block or dilation and S_kv a multiple of 128), so the
 // element-wise mask code is left out of the kernel. SEG: packed sequences.
 template <int D, bool BF16, int KIND, bool MASKED, bool SEG>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D, fmha2_parts(KIND)>::THREADS, 1)
     fmha2_fwd_kernel(const __grid_constant__ CUtensorMap tm_q,
                      const __grid_constant__ CUtensorMap tm_kh,
                      const __grid_constant__ CUtensorMap tm_vh,
                      const __grid_constant__ CUtensorMap tm_o, const KernelArgs args) {
-  using C = Fmha2Config<D>;
+  using C = Fmha2Config<D, fmha2_parts(KIND)>;
   constexpr int BM = C::BM, BN = C::BN, NKV = C::NKV;
   constexpr bool SOFTMAX = (KIND == KIND_SOFTMAX || KIND == KIND_SOFTCAP || KIND == KIND_ALIBI);
 
@@ -566,8 +627,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       uint32_t at[8];
       uint64_t bd[8];
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {  // P of keys 16kk.. at column 8kk (+32 past key 64)
-        at[kk] = p_tmem + kk * 8 + (kk >= 4 ? 32 : 0);
+      for (int kk = 0; kk < 8; ++kk) {  // P of keys 16kk.. inside their part's S columns
+        at[kk] = p_tmem + (kk * 16 / C::COLS) * C::COLS + (kk * 16 % C::COLS) / 2;
         bd[kk] = b0 + ((kk * 2048) >> 4);
       }
       ptx::umma_ts_2sm_x8_warp(d_tmem, at, bd, IDESC_PV, first ? 0u : 1u);
@@ -637,10 +698,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
     __syncwarp();
   } else if (warp < C::SOFTMAX_WARPS) {
     // ======================= softmax / epilogue =======================
-    const int quad = warp & 3, half = warp >> 2;
+    constexpr int NP = C::NP, COLS = C::COLS, CH = C::CH;
+    const int quad = warp & 3, part = warp >> 2;
     const int row = quad * 32 + lane;  // TMEM lane = query row in this CTA's tile
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    const uint32_t tO = tmem_base + lane_off + C::TMEM_O + half * 64;
+    const uint32_t tO = tmem_base + lane_off + C::TMEM_O + part * COLS;
     const int prefix = static_cast<int>(g.prefix);
     const int dil = static_cast<int>(g.dil);
     uint32_t dil_pat = 0u;  // a bit at every multiple of the dilation below 32
@@ -649,16 +711,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
     float *xch = reinterpret_cast<float *>(smem + C::OFF_XCH);
     uint32_t xcnt = 0;
     // Exchange of one float per row with the warp that owns the other column
-    // half of these rows: publish() hands v over without waiting, collect()
-    // returns the other warp's value of the same exchange. Both warps publish
-    // and collect in the same order. Two slots per quadrant keep a fast warp
-    // from overwriting a value the other has not read: a warp publishes
-    // exchange n+2 only after collecting n+1, which the other publishes only
-    // after collecting n. collect() waits with a bound: false means the
-    // kernel is aborting.
+    // part of these rows (softmax kinds, two parts): publish() hands v over
+    // without waiting, collect() returns the other warp's value of the same
+    // exchange. Both warps publish and collect in the same order. Two slots
+    // per quadrant keep a fast warp from overwriting a value the other has
+    // not read: a warp publishes exchange n+2 only after collecting n+1,
+    // which the other publishes only after collecting n. collect() waits
+    // with a bound: false means the kernel is aborting.
+    static_assert(!SOFTMAX || C::EXCHANGE, "softmax kinds run with two column parts");
     auto publish = [&](float v) {
       const uint32_t slot = xcnt & 1;
-      xch[slot * 256 + half * 128 + row] = v;
+      xch[slot * 256 + (part & 1) * 128 + row] = v;
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar(C::BAR_XCH + quad * 2 + slot));
     };
@@ -666,15 +729,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       const uint32_t slot = xcnt & 1, phase = (xcnt >> 1) & 1;
       ++xcnt;
       if (!bounded_wait(wc, bar(C::BAR_XCH + quad * 2 + slot), phase)) return false;
-      other = xch[slot * 256 + (half ^ 1) * 128 + row];
+      other = xch[slot * 256 + ((part & 1) ^ 1) * 128 + row];
       return true;
     };
-    auto exchange = [&](float v, float &other) -> bool {
-      publish(v);
-      return collect(other);
-    };
     Tracer tr(warp == 0 ? 0 : 1);
-    const bool tracing = warp == 0 && lane == 0;
+    const bool tracing = (warp == 0 || warp == 4) && lane == 0;
     auto trs = [&](int tag) { if (tracing) tr(tag); };
     uint32_t cnt = 0;  // tiles seen (all tiles of every unit)
     uint32_t units = 0;
@@ -694,13 +753,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
         // (nothing is staged for the load thread to store).
         if (i < g.sq) {
           const int64_t real_row = static_cast<int64_t>(i) * args.vdil + U.r_res;
-          if (SOFTMAX && args.lse != nullptr && half == 0)
+          if (SOFTMAX && args.lse != nullptr && part == 0)
             store_lse(args, U.b, U.h, real_row, -INFINITY, 0.f);
           uint8_t *orow = reinterpret_cast<uint8_t *>(args.o) +
                           2 * (U.b * args.o_sb + static_cast<int64_t>(U.h) * args.o_sh +
-                               real_row * args.o_ss + half * 64);
+                               real_row * args.o_ss + part * COLS);
 #pragma unroll
-          for (int v4 = 0; v4 < 8; ++v4) ptx::st_global_v4(orow + v4 * 16, 0u, 0u, 0u, 0u);
+          for (int v4 = 0; v4 < COLS / 8; ++v4) ptx::st_global_v4(orow + v4 * 16, 0u, 0u, 0u, 0u);
         }
         continue;
       }
@@ -716,7 +775,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       for (int k2 = 0; k2 < U.tiles; ++k2, ++cnt) {
         const int t = U.rev ? U.jlo + U.tiles - 1 - k2 : U.jlo + k2;
         const uint32_t buf = cnt % C::NSBUF;
-        const uint32_t tS = tmem_base + lane_off + buf * 128 + half * 64;
+        const uint32_t tS = tmem_base + lane_off + buf * 128 + part * COLS;
         if (!bounded_wait(wc, bar(C::BAR_SFULL + buf), (cnt / C::NSBUF) & 1)) {
           ok = false;
           break;
@@ -724,16 +783,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
         trs(10);
         ptx::tc_fence_after();
         if (t >= U.tlo && t < U.thi) {  // this CTA's query tile sees key tile t
-          uint32_t sr[2][32];
+          uint32_t sr[CH][32];
           if (SOFTMAX) {
-            ptx::tmem_ld32(tS, sr[0]);
-            ptx::tmem_ld32(tS + 32, sr[1]);
+#pragma unroll
+            for (int c = 0; c < CH; ++c) ptx::tmem_ld32(tS + 32 * c, sr[c]);
             ptx::tmem_wait_ld();
-            ptx::reg_fence(sr[0]);
-            ptx::reg_fence(sr[1]);
+#pragma unroll
+            for (int c = 0; c < CH; ++c) ptx::reg_fence(sr[c]);
           }
           trs(11);
-          const int kv0 = static_cast<int>(t) * BN + half * 64;  // key of column 0 of sr
+          const int kv0 = static_cast<int>(t) * BN + part * COLS;  // key of column 0 of sr
           RowMask rm;
           rm.c_lo = blo - kv0;
           rm.span = span;
@@ -742,30 +801,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
           rm.dil = dil;
           kc.rel0 = static_cast<float>(kv0 - i);
           const int mode = (!MASKED || ft.full(t)) ? 0 : (dil == 1 ? 1 : 2);
-          const PSinkTmem sink{tS};  // P of these 64 keys -> first 32 of these columns
           if (SOFTMAX) {
-            float mx;
             uint32_t skip = 0u;  // chunks of a masked tile no row of this warp sees
-            if (mode == 0)
-              mx = softmax_pass1<KIND, 0, 2>(sr, kc, rm);
-            else
-              mx = softmax_pass1_masked<KIND>(sr, kc, rm, dil_pat, skip);
-            auto pass2 = [&](float m) -> float {
-              return skip == 0u ? softmax_pass2<BF16>(sr, m, sink)
-                                : softmax_pass2_skip<BF16>(sr, m, skip, tS);
-            };
-            // The row maximum of the whole tile needs the other half's. After
+            const float mx = mode == 0 ? softmax_pass1_cols<KIND, CH, false>(sr, kc, rm, dil_pat, skip)
+                                       : softmax_pass1_cols<KIND, CH, true>(sr, kc, rm, dil_pat, skip);
+            // The row maximum of the whole tile needs the other parts'. After
             // the first tile, P is computed optimistically against the running
             // maximum, which stays exact unless the maximum grew by more than
-            // 2^8 (lazy rescale); the other half's value is collected only
-            // afterwards, when it has long been published.
+            // 2^8 (lazy rescale); the other parts' values are collected only
+            // afterwards, when they have long been published.
             publish(mx);
             float lsum = 0.f;
-            if (!first_mine) lsum = pass2(m_run == -INFINITY ? 0.f : m_run);
+            if (!first_mine)
+              lsum = softmax_pass2_cols<BF16, CH>(sr, m_run == -INFINITY ? 0.f : m_run, skip, tS);
             float mx_other;
             if (!collect(mx_other)) { ok = false; break; }
-            mx = fmaxf(mx, mx_other);  // row maximum over the whole tile
-            const float m_new = fmaxf(m_run, mx);
+            const float m_new = fmaxf(m_run, fmaxf(mx, mx_other));  // row maximum, whole tile
             const bool need = m_new > m_run + 8.0f;
             if (first_mine || __any_sync(0xffffffffu, need)) {
               float alpha = 1.0f;
@@ -783,28 +834,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
                   break;
                 }
                 ptx::tc_fence_after();
-                rescale_rows<64>(tO, alpha);
+                rescale_rows<COLS>(tO, alpha);
               }
               // (re)compute P against the new maximum; P is not yet signalled
-              lsum = pass2(m_run == -INFINITY ? 0.f : m_run);
+              lsum = softmax_pass2_cols<BF16, CH>(sr, m_run == -INFINITY ? 0.f : m_run, skip, tS);
             }
             l_run += lsum;
           } else {
             if (mode == 0)
-              pointwise_tmem64<KIND, 0, BF16>(tS, kc, rm);
+              pointwise_tmem_cols<KIND, 0, BF16, CH>(tS, kc, rm);
             else if (mode == 1)
-              pointwise_tmem64<KIND, 1, BF16>(tS, kc, rm);
+              pointwise_tmem_cols<KIND, 1, BF16, CH>(tS, kc, rm);
             else
-              pointwise_tmem64<KIND, 2, BF16>(tS, kc, rm);
+              pointwise_tmem_cols<KIND, 2, BF16, CH>(tS, kc, rm);
           }
           first_mine = false;
           trs(12);
         } else {
           // the pair computes this tile for the other query tile only: P = 0 here
-          uint32_t z[32];
-#pragma unroll
-          for (int e = 0; e < 32; ++e) z[e] = 0u;
-          ptx::tmem_st32(tS, z);
+          tmem_zero_cols<CH>(tS);
         }
         ptx::tmem_wait_st();
         trs(16);  // P stores retired
@@ -823,11 +871,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       float inv;
       if (SOFTMAX) {
         float l_other;
-        if (!exchange(l_run, l_other)) break;
-        const float l_tot = l_run + l_other;
+        publish(l_run);
+        if (!collect(l_other)) break;
+        // in part order, so both parts hold the same bits
+        const float l_tot = part == 0 ? l_run + l_other : l_other + l_run;
         inv = (l_tot > 0.f) ? 1.0f / l_tot : 0.f;
-        // both halves hold the same running maximum (they agree on every tile's)
-        if (args.lse != nullptr && half == 0 && i < g.sq)
+        // every part holds the same running maximum (they agree on every tile's)
+        if (args.lse != nullptr && part == 0 && i < g.sq)
           store_lse(args, U.b, U.h, static_cast<int64_t>(i) * args.vdil + U.r_res, m_run, l_tot);
       } else if (KIND == KIND_RELU) {
         inv = args.out_scale;
@@ -837,27 +887,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D>::THRE
       if (!bounded_wait(wc, bar(C::BAR_OFULL), units & 1)) break;  // units with key tiles
       ptx::tc_fence_after();
       trs(14);
-      uint32_t o[2][32];
-      ptx::tmem_ld32(tO, o[0]);
-      ptx::tmem_ld32(tO + 32, o[1]);
+      uint32_t o[CH][32];
+#pragma unroll
+      for (int c = 0; c < CH; ++c) ptx::tmem_ld32(tO + 32 * c, o[c]);
       ptx::tmem_wait_ld();
-      ptx::reg_fence(o[0]);
-      ptx::reg_fence(o[1]);
+#pragma unroll
+      for (int c = 0; c < CH; ++c) ptx::reg_fence(o[c]);
       // O is in registers: the MMA may start the next unit's PV
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive_remote(oempty);
-      // stage this row's 64 columns (16-bit) in the unit's Q buffer, column
-      // chunk `half`, in the 128-byte swizzle of the output tensor map
-      uint32_t pk[32];
+      // stage this row's COLS columns (16-bit) in the unit's Q buffer (column
+      // chunk part * COLS / 64, 16-byte units from (part * COLS % 64) / 8), in
+      // the 128-byte swizzle of the output tensor map
+      uint32_t pk[CH * 16];
 #pragma unroll
-      for (int c = 0; c < 2; ++c)
+      for (int c = 0; c < CH; ++c)
 #pragma unroll
         for (int e = 0; e < 16; ++e)
           pk[c * 16 + e] = pack2<BF16>(__uint_as_float(o[c][2 * e]) * inv,
                                        __uint_as_float(o[c][2 * e + 1]) * inv);
-      const uint32_t qbuf = sbase + C::OFF_Q + slot * C::Q_BYTES + half * C::Q_CHUNK;
-      store_p_chunk(qbuf + row * 128, 0, row & 7, pk);
+      const uint32_t qrow = sbase + C::OFF_Q + slot * C::Q_BYTES +
+                            (part * COLS / 64) * C::Q_CHUNK + row * 128;
+      const int u0 = (part * COLS % 64) / 8;
+#pragma unroll
+      for (int u = 0; u < COLS / 8; ++u)
+        ptx::st_shared_v4(qrow + (((u0 + u) ^ (row & 7)) << 4), pk[4 * u], pk[4 * u + 1],
+                          pk[4 * u + 2], pk[4 * u + 3]);
       ptx::fence_proxy_async_smem();  // visible to the TMA store
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar(C::BAR_OSTAGED + slot));
