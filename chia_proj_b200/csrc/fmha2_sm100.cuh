@@ -698,7 +698,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D, fmha2
     __syncwarp();
   } else if (warp < C::SOFTMAX_WARPS) {
     // ======================= softmax / epilogue =======================
-    constexpr int NP = C::NP, COLS = C::COLS, CH = C::CH;
+    constexpr int COLS = C::COLS, CH = C::CH;
     const int quad = warp & 3, part = warp >> 2;
     const int row = quad * 32 + lane;  // TMEM lane = query row in this CTA's tile
     const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
