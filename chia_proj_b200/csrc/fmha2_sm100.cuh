@@ -882,7 +882,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D, fmha2
       } else if (KIND == KIND_RELU) {
         inv = args.out_scale;
       } else {
-        inv = 1.0f;
+        inv = pointwise_out_scale<BF16>(KIND);
       }
       if (!bounded_wait(wc, bar(C::BAR_OFULL), units & 1)) break;  // units with key tiles
       ptx::tc_fence_after();

@@ -345,13 +345,24 @@ __device__ __forceinline__ float softmax_pass2(uint32_t (&sr)[NC][32], float m, 
 // Non-softmax kinds: P = relu(s * scale) or sigmoid(s * scale + bias),
 // masked, packed and handed to the P sink.
 // Sigmoid is 1 / (1 + 2^t): 2^t on the MUFU, the reciprocal on the FMA pipe:
-// an initial guess r0 = as_float(0x7EF311C2 - bits(y)) and two Newton steps
+// an initial guess r0 = as_float(0x7EF311C2 - bits(y)) and Newton steps
 // r <- r (2 - y r). The constant minimises the largest relative error of r0
-// over all y (0.0505; the search is recip_seed.py beside this file), so after
-// two steps the error is about 0.0505^4 = 6.5e-6, far below the 2^-9 rounding
-// of the 16-bit P. y is negated here (-(1 + 2^t)), hence 0xFEF311C2 - bits.
+// over all y (0.0505; the search is recip_seed.py beside this file). One step
+// leaves a one-sided error 1 - y r in [0, 0.0505^2 = 2.55e-3]; the epilogue
+// multiplies O by kSigmoidCentre = 1 / (1 - 2.55e-3 / 2), which centres it to
+// +-1.28e-3, below the rounding of a bf16 P (2^-9 .. 2^-8 relative). fp16 P
+// rounds to 2^-11, so fp16 takes a second step (error 0.0505^4 = 6.5e-6).
+// y is negated here (-(1 + 2^t)), hence 0xFEF311C2 - bits.
 // One 32-column chunk (src, columns col0..col0+31 of the tile) of the
 // pointwise kinds, as 16 packed pairs into pk[off .. off+15].
+// Output scale that centres the one-sided error of the single Newton step
+// of a bf16 sigmoid P (see pointwise_chunk): 1 / (1 - 0.0505^2 / 2).
+constexpr float kSigmoidCentre = 1.001277273908313f;
+template <bool BF16>
+__device__ __forceinline__ constexpr float pointwise_out_scale(int kind) {
+  return (kind == KIND_SIGMOID && BF16) ? kSigmoidCentre : 1.0f;
+}
+
 template <int KIND, int MODE, bool BF16>
 __device__ __forceinline__ void pointwise_chunk(const uint32_t (&src)[32], int col0,
                                                 const EpiConsts &k, const RowMask &rm,
@@ -383,7 +394,7 @@ __device__ __forceinline__ void pointwise_chunk(const uint32_t (&src)[32], int c
       uint64_t r = ptx::f2(__uint_as_float(0xFEF311C2u - __float_as_uint(y0)),
                            __uint_as_float(0xFEF311C2u - __float_as_uint(y1)));
       r = ptx::mul2(r, ptx::fma2(ny, r, TWO2));
-      r = ptx::mul2(r, ptx::fma2(ny, r, TWO2));
+      if (!BF16) r = ptx::mul2(r, ptx::fma2(ny, r, TWO2));
       ptx::f2_split(r, a, b);
       if (MODE != 0) {
         if (!col_visible<MODE>(rm, col)) a = 0.f;
@@ -988,7 +999,7 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
       else if (KIND == KIND_RELU)
         inv = args.out_scale;
       else
-        inv = 1.0f;
+        inv = pointwise_out_scale<BF16>(KIND);
       const bool row_ok = i < g.sq;
       const int64_t real_row = static_cast<int64_t>(i) * args.vdil + U.r_res;
       uint8_t *orow = reinterpret_cast<uint8_t *>(args.o) +

@@ -5,10 +5,16 @@ pipe: an initial guess from integer arithmetic on the IEEE-754 bits,
 
     r0 = as_float(C - bits(y)),
 
-followed by two Newton-Raphson steps r <- r * (2 - y * r). Subtracting the
-bits from a constant negates the exponent field (and, approximately, the
+followed by Newton-Raphson steps r <- r * (2 - y * r). Subtracting the bits
+from a constant negates the exponent field (and, approximately, the
 mantissa), so r0 is within a few per cent of 1/y for every y. One Newton step
-squares the relative error e = 1 - y*r, so after two steps it is e0^4.
+squares the relative error e = 1 - y*r: after one step it lies in
+[0, e0_max^2], after two in [0, e0_max^4].
+
+A bf16 P takes one step and the epilogue scales the output by
+1 / (1 - e0_max^2 / 2) (``centre_scale``), which moves the one-sided error to
++-e0_max^2 / 2 = 1.28e-3, below the rounding of a bf16 value (2^-9 to 2^-8
+relative). An fp16 P (rounding 2^-11) takes both steps.
 
 C is chosen here as the value that minimises the largest relative error
 max |1 - y*r0| of the seed. The seed's relative error depends on the mantissa
@@ -42,13 +48,18 @@ def seed_error(c: int, step: int = 1) -> float:
     return float(np.max(np.abs(1.0 - y * r0)))
 
 
-def sigmoid_recip(y: np.ndarray, c: int = KERNEL_SEED) -> np.ndarray:
+def centre_scale(c: int = KERNEL_SEED) -> float:
+    """Output scale that centres the one-sided error of one Newton step."""
+    return 1.0 / (1.0 - seed_error(c) ** 2 / 2.0)
+
+
+def sigmoid_recip(y: np.ndarray, c: int = KERNEL_SEED, steps: int = 2) -> np.ndarray:
     """The kernel's reciprocal of y >= 1 in single precision: the seed and
-    two Newton steps r * fma(-y, r, 2), each fused multiply-add formed in
+    ``steps`` Newton steps r * fma(-y, r, 2), each fused multiply-add formed in
     double precision and rounded once to single."""
     y = np.asarray(y, dtype=np.float32)
     r = (np.uint32(c) - y.view(np.uint32)).view(np.float32)
-    for _ in range(2):
+    for _ in range(steps):
         corr = (-(y.astype(np.float64)) * r.astype(np.float64) + 2.0).astype(np.float32)
         r = (r * corr).astype(np.float32)
     return r
@@ -77,3 +88,5 @@ def search() -> tuple[int, float]:
 if __name__ == "__main__":
     c, e = search()
     print(f"seed constant 0x{c:08X}: seed error {e:.6f}, after two Newton steps {e ** 4:.3e}")
+    print(f"one step: error in [0, {e ** 2:.4e}]; centring scale {centre_scale(c)!r} "
+          f"leaves +-{e ** 2 / 2:.4e}")
