@@ -819,6 +819,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D, fmha2
             const float m_new = fmaxf(m_run, fmaxf(mx, mx_other));  // row maximum, whole tile
             const bool need = m_new > m_run + 8.0f;
             if (first_mine || __any_sync(0xffffffffu, need)) {
+              // A row that has seen no key yet (m_run = -inf) has a zero O row
+              // and l_run = 0: it takes the new maximum without a rescale of O.
+              const bool need_o = need && m_run != -INFINITY;
               float alpha = 1.0f;
               if (need) {
                 alpha = ptx::ex2(m_run - m_new);
@@ -827,14 +830,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fmha2Config<D, fmha2
               }
               if (!first_mine) {
                 ptx::tmem_wait_st();  // the optimistic P is written before it is replaced
-                // O holds every earlier PV once PV(t-1) retired (it frees that stage)
-                const uint32_t prev = cnt - 1;
-                if (!bounded_wait(wc, bar(C::BAR_KVEMPTY + prev % NKV), (prev / NKV) & 1)) {
-                  ok = false;
-                  break;
+                if (__any_sync(0xffffffffu, need_o)) {
+                  // O holds every earlier PV once PV(t-1) retired (it frees that stage)
+                  const uint32_t prev = cnt - 1;
+                  if (!bounded_wait(wc, bar(C::BAR_KVEMPTY + prev % NKV), (prev / NKV) & 1)) {
+                    ok = false;
+                    break;
+                  }
+                  ptx::tc_fence_after();
+                  rescale_rows<COLS>(tO, alpha);
                 }
-                ptx::tc_fence_after();
-                rescale_rows<COLS>(tO, alpha);
               }
               // (re)compute P against the new maximum; P is not yet signalled
               lsum = softmax_pass2_cols<BF16, CH>(sr, m_run == -INFINITY ? 0.f : m_run, skip, tS);

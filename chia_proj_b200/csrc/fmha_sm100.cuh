@@ -962,13 +962,15 @@ __global__ void __launch_bounds__(FmhaConfig<D>::THREADS, 1)
           ptx::tc_fence_after();
           const float m_new = fmaxf(m_run, mx);
           const bool need = m_new > m_run + 8.0f;
+          // a row that has seen no key yet has a zero O row: no rescale
+          const bool need_o = need && m_run != -INFINITY;
           float alpha = 1.0f;
           if (need) {
             alpha = ptx::ex2(m_run - m_new);
             l_run *= alpha;
             m_run = m_new;
           }
-          if (t > U.tlo[w] && __any_sync(0xffffffffu, need)) rescale_rows<D>(tO, alpha);
+          if (t > U.tlo[w] && __any_sync(0xffffffffu, need_o)) rescale_rows<D>(tO, alpha);
           const float m_use = (m_run == -INFINITY) ? 0.0f : m_run;
           l_run += softmax_pass2<BF16>(sr, m_use, PSinkSmem{prow, rsw});
         } else {
