@@ -354,7 +354,11 @@ __device__ __forceinline__ float softmax_pass2(uint32_t (&sr)[NC][32], float m, 
 // multiplies O by kSigmoidCentre = 1 / (1 - 2.55e-3 / 2), which centres it to
 // +-1.28e-3, below the rounding of a bf16 P (2^-9 .. 2^-8 relative). fp16 P
 // rounds to 2^-11, so fp16 takes a second step (error 0.0505^4 = 6.5e-6).
-// y is negated here (-(1 + 2^t)), hence 0xFEF311C2 - bits.
+// y is negated and quartered here, y = -(1 + 2^t) / 4 (hence 0xFEF311C2 -
+// bits), so r and P are 4 sigmoid and the epilogue's output scale takes the
+// 4 back. The quarter keeps bits(y) below the seed constant for every finite
+// 2^t, so no clamp of t is needed: 2^t = inf (t >= 128) gives r = -inf,
+// which the ReLU form of the conversion packs as 0, the limit of sigmoid.
 // One 32-column chunk (src, columns col0..col0+31 of the tile) of the
 // pointwise kinds, as 16 packed pairs into pk[off .. off+15].
 // Output scale that centres the one-sided error of the single Newton step
@@ -362,7 +366,7 @@ __device__ __forceinline__ float softmax_pass2(uint32_t (&sr)[NC][32], float m, 
 constexpr float kSigmoidCentre = 1.001277273908313f;
 template <bool BF16>
 __device__ __forceinline__ constexpr float pointwise_out_scale(int kind) {
-  return (kind == KIND_SIGMOID && BF16) ? kSigmoidCentre : 1.0f;
+  return kind == KIND_SIGMOID ? (BF16 ? 0.25f * kSigmoidCentre : 0.25f) : 1.0f;
 }
 
 template <int KIND, int MODE, bool BF16>
@@ -371,7 +375,7 @@ __device__ __forceinline__ void pointwise_chunk(const uint32_t (&src)[32], int c
                                                 uint32_t (&pk)[32], int off) {
   const uint64_t K2 = ptx::f2(k.k_mul, k.k_mul);
   const uint64_t KB2 = ptx::f2(k.k_bias, k.k_bias);
-  const uint64_t NEG1 = ptx::f2(-1.0f, -1.0f);
+  const uint64_t NEGQ = ptx::f2(-0.25f, -0.25f);
   const uint64_t TWO2 = ptx::f2(2.0f, 2.0f);
 #pragma unroll
   for (int e = 0; e < 32; e += 2) {
@@ -386,11 +390,11 @@ __device__ __forceinline__ void pointwise_chunk(const uint32_t (&src)[32], int c
       }
       pk[off + e / 2] = BF16 ? ptx::pack_bf16_relu(a, b) : ptx::pack_f16_relu(a, b);
     } else {
-      // t = -(s*scale + bias) * log2(e), clamped so 2^t stays finite
+      // t = -(s*scale + bias) * log2(e)
       float t0, t1;
       ptx::f2_split(ptx::fma2(s2, K2, KB2), t0, t1);
-      const uint64_t e2 = ptx::f2(ptx::ex2(fminf(t0, 126.f)), ptx::ex2(fminf(t1, 126.f)));
-      const uint64_t ny = ptx::fma2(e2, NEG1, NEG1);  // -(1 + 2^t)
+      const uint64_t e2 = ptx::f2(ptx::ex2(t0), ptx::ex2(t1));
+      const uint64_t ny = ptx::fma2(e2, NEGQ, NEGQ);  // -(1 + 2^t) / 4
       float y0, y1;
       ptx::f2_split(ny, y0, y1);
       uint64_t r = ptx::f2(__uint_as_float(0xFEF311C2u - __float_as_uint(y0)),
@@ -402,7 +406,7 @@ __device__ __forceinline__ void pointwise_chunk(const uint32_t (&src)[32], int c
         if (!col_visible<MODE>(rm, col)) a = 0.f;
         if (!col_visible<MODE>(rm, col + 1)) b = 0.f;
       }
-      pk[off + e / 2] = pack2<BF16>(a, b);
+      pk[off + e / 2] = BF16 ? ptx::pack_bf16_relu(a, b) : ptx::pack_f16_relu(a, b);
     }
   }
 }

@@ -424,6 +424,24 @@ def test_running_max_rises_every_tile(cuda, op, D, kw):
         assert torch.equal(out, run(op, q, k, v, **kw))
 
 
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("causal", [False, True])
+def test_sigmoid_logits_whose_exponential_overflows(cuda, D, dtype, causal):
+    """Scores of spread 20 with bias -60: t = -(s - 60) log2(e) runs from
+    about 0 to 200, so 2^t overflows to inf for roughly a tenth of the pairs
+    (sigmoid there is below 1e-38) while the rest span the whole curve. Each
+    such P must come out 0, every other one as in the oracle."""
+    q, k, v = gen(1, 4, 640, D, dtype, seed=43)
+    q, k = ((x.float() * math.sqrt(20.0)).to(dtype) for x in (q, k))  # s ~ N(0, 20^2)
+    kw = dict(causal=causal, bias=-60.0)
+    s = (q.float() @ k.float().transpose(-2, -1)) / math.sqrt(D)
+    t = -(s - 60.0) * math.log2(math.e)
+    assert (t >= 128).float().mean() > 0.02 and (t < 40).float().mean() > 0.02
+    check(run("sigmoid_attn", q, k, v, **kw), oracle.run_op("sigmoid_attn", q, k, v, **kw),
+          f"sigmoid overflow D={D}")
+
+
 @pytest.mark.parametrize("S", [1024, 1000])
 @pytest.mark.parametrize("op,kw", [("softcap_gemma2", dict(cap=50.0, causal=False)),
                                    ("sigmoid_attn", dict(causal=False, bias=-2.0)),
