@@ -360,16 +360,19 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
             if nbytes < 0:
                 raise ValueError("not a decode-shaped call")
             ws = _decode_workspace(dev, stream, nbytes)
-            N.check(lib.chia_attn_decode(ctypes.byref(p), ctypes.c_void_p(ws.data_ptr()),
-                                         ws.numel(), ctypes.c_void_p(stream)),
-                    f"chia_attn_decode(norm={norm}, mod={mod}, mask={mask}, "
-                    f"q={tuple(q.shape)}, k={tuple(k.shape)})")
+            code = lib.chia_attn_decode(ctypes.byref(p), ctypes.c_void_p(ws.data_ptr()),
+                                        ws.numel(), ctypes.c_void_p(stream))
+            if code:  # the message is formatted only on failure (host time per call)
+                N.check(code, f"chia_attn_decode(norm={norm}, mod={mod}, mask={mask}, "
+                              f"q={tuple(q.shape)}, k={tuple(k.shape)})")
             o = o.float() if in_dtype == torch.float32 else o
             return (o, lse) if return_lse else o
         # one workspace per (device, stream): see _workspace
         p.workspace = _workspace(dev, stream).data_ptr() if schedule == "dynamic" else None
-        N.check(lib.chia_attn_fwd(ctypes.byref(p), ctypes.c_void_p(stream)),
-                f"chia_attn_fwd(norm={norm}, mod={mod}, mask={mask}, shape={tuple(q.shape)})")
+        code = lib.chia_attn_fwd(ctypes.byref(p), ctypes.c_void_p(stream))
+        if code:  # the message is formatted only on failure (host time per call)
+            N.check(code, f"chia_attn_fwd(norm={norm}, mod={mod}, mask={mask}, "
+                          f"shape={tuple(q.shape)})")
     o = o.float() if in_dtype == torch.float32 else o
     return (o, lse) if return_lse else o
 
@@ -441,9 +444,11 @@ def attention_backward(dout, q, k, v, out, lse, *, norm="softmax", mod="none", m
         if ws is None or ws.numel() < nbytes:
             ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
             _bwd_workspaces[key] = ws
-        N.check(lib.chia_attn_bwd(ctypes.byref(p), ctypes.byref(g), ctypes.c_void_p(ws.data_ptr()),
-                                  ws.numel(), ctypes.c_void_p(stream)),
-                f"chia_attn_bwd(norm={norm}, mod={mod}, mask={mask}, shape={tuple(q.shape)})")
+        code = lib.chia_attn_bwd(ctypes.byref(p), ctypes.byref(g), ctypes.c_void_p(ws.data_ptr()),
+                                 ws.numel(), ctypes.c_void_p(stream))
+        if code:  # the message is formatted only on failure
+            N.check(code, f"chia_attn_bwd(norm={norm}, mod={mod}, mask={mask}, "
+                          f"shape={tuple(q.shape)})")
     return dq, dk, dv
 
 
